@@ -1,0 +1,436 @@
+#!/usr/bin/env python
+"""bpt benchmark: achieved HBM bandwidth of paged-KV GQA decode on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl bpt|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU, NCCL)
+
+A step is one single-layer decode call over one batch (Llama-3-8B layer: Hq=32, Hkv=8, D=128)
+of synthetic paged KV with seeded ragged lengths and a random-permutation block table, inputs
+resident in HBM. Multi-GPU runs shard by batch (each rank owns its own batch and KV pool, no
+collective on the data path): weak scaling; the time is the max over ranks.
+
+Prints ONE JSON line (rank 0). `value` is the whole-job achieved bandwidth in TB/s:
+algorithmic bytes of all ranks' calls / max-over-ranks device time. `roofline` reports the
+dominant kernel (the split-KV decode kernel) against the measured HBM copy peak. `e2e` is the
+same metric through the public API with per-step host->device copies of the step's inputs
+(q, block table, sequence lengths) from pinned memory and a device->host read of the output;
+the KV cache is resident state, like weights. `--impl reference` times the reference's CPU
+algorithm (the numpy port in oracle/) on the host cores on a bounded sample of the workload.
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "kvq-decode_b200"))
+sys.path.insert(0, ROOT)
+
+HQ, HKV, D = 32, 8, 128
+FALLBACK_HBM_GBS = 6650.0
+B200_SPEC_GBS = 8000.0
+
+# BASELINE configs[1] (FP16 batch) and configs[2] (FP16 batch 1); default = the largest
+# single-GPU configuration of the FP16 batch family.
+WORKLOADS = {
+    "fp16_b64_ctx64k": dict(fmt="fp16", batch=64, ctx=65536, block_size=16, ragged=True),
+    "fp16_b32_ctx64k": dict(fmt="fp16", batch=32, ctx=65536, block_size=16, ragged=True),
+    "fp16_b16_ctx64k": dict(fmt="fp16", batch=16, ctx=65536, block_size=16, ragged=True),
+    "fp16_b8_ctx64k": dict(fmt="fp16", batch=8, ctx=65536, block_size=16, ragged=True),
+    "fp16_b64_ctx16k": dict(fmt="fp16", batch=64, ctx=16384, block_size=16, ragged=True),
+    "fp16_b32_ctx16k": dict(fmt="fp16", batch=32, ctx=16384, block_size=16, ragged=True),
+    "fp16_b16_ctx16k": dict(fmt="fp16", batch=16, ctx=16384, block_size=16, ragged=True),
+    "fp16_b8_ctx16k": dict(fmt="fp16", batch=8, ctx=16384, block_size=16, ragged=True),
+    "fp16_b1_ctx4k": dict(fmt="fp16", batch=1, ctx=4096, block_size=16, ragged=False),
+    "fp16_b1_ctx16k": dict(fmt="fp16", batch=1, ctx=16384, block_size=16, ragged=False),
+    "fp16_b1_ctx64k": dict(fmt="fp16", batch=1, ctx=65536, block_size=16, ragged=False),
+    "fp16_b1_ctx128k": dict(fmt="fp16", batch=1, ctx=131072, block_size=16, ragged=False),
+}
+DEFAULT_WORKLOAD = "fp16_b64_ctx64k"
+# published reference number for the same metric (A100-80GB, best split, B=32 ctx=16k,
+# docs/NOTES.md:99 of the reference): 1638 GB/s
+REFERENCE_PUBLISHED_TBPS = 1.638
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["bpt", "reference"], default="bpt")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
+    ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0,
+                    help="budget of the CPU-baseline sample")
+    return ap.parse_args()
+
+
+def workload_lens(wl, rank, seed):
+    from bpt.cache import ragged_lengths
+    if wl["ragged"]:
+        return ragged_lengths(wl["batch"], wl["ctx"], seed + 7919 * rank)
+    return [wl["ctx"]] * wl["batch"]
+
+
+def config_dict(name, wl, n_gpus):
+    return {
+        "workload": f"{name}: BASELINE configs[{1 if wl['batch'] > 1 else 2}] "
+                    f"{wl['fmt']} paged KV, Llama-3-8B layer (Hq={HQ}, Hkv={HKV}, D={D}), "
+                    f"B={wl['batch']} per GPU, ctx={wl['ctx']}"
+                    + (" seq_len~U[0.75ctx,ctx]" if wl["ragged"] else "")
+                    + f", block_size={wl['block_size']}, random-permutation block table",
+        "kv_dtype": wl["fmt"], "batch_per_gpu": wl["batch"], "ctx": wl["ctx"],
+        "block_size": wl["block_size"], "q_heads": HQ, "kv_heads": HKV, "head_dim": D,
+        "parallelism": f"batch-sharded x{n_gpus} (independent sequences per rank)",
+        "l2": "no flush: per-step working set (GBs of KV) far exceeds the 126 MB L2",
+    }
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs, STREAM copy)"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback (no MEASURED_PEAKS.json)"
+
+
+def ncu_traffic(workload):
+    """DRAM bytes per launch of the split kernel from a committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", "dram_traffic.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        e = d.get(workload)
+        return (float(e["bytes_per_launch"]), e.get("note")) if e else (None, None)
+    except Exception:
+        return None, None
+
+
+class ClockSampler:
+    """NVML SM-clock and clock-event-reason sampling while the timed region runs."""
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+               0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x100: "display_clock_setting"}
+
+    def __init__(self, device_index):
+        self.samples, self.reasons, self.ok = [], 0, False
+        self._stop = threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = self._handle(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # pragma: no cover - NVML missing
+            self.err = str(e)
+
+    def _handle(self, idx):
+        import torch
+        try:
+            p = torch.cuda.get_device_properties(idx)
+            bus = f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
+            return self.nv.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return self.nv.nvmlDeviceGetHandleByIndex(idx)
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            except Exception:
+                pass
+            time.sleep(0.002)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.ok:
+            self._stop.set()
+            self.t.join()
+
+    def summary(self):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": self.err}
+        names = [v for k, v in self.REASONS.items() if self.reasons & k and k != 0x1]
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(self.samples)}
+
+
+# ----------------------------------------------------------------------------- CPU oracle
+
+def cpu_oracle_sample(lens, block_size, seed, budget_s, k_pages_fn=None):
+    """Time the numpy oracle (reference algorithm, src/bpt/reference.py:20-49) on a bounded
+    sample: whole sequences of the workload's length distribution, until ~budget_s seconds.
+    Returns (GB/s, seconds, bytes, description)."""
+    import numpy as np
+    from bpt.roofline import decode_call_bytes
+    from oracle import attention as oa
+    g = np.random.Generator(np.random.PCG64(seed))
+    n = int(lens[0])
+    pages = (n + block_size - 1) // block_size
+    kc = g.standard_normal((pages, block_size, HKV, D), dtype=np.float32).astype(np.float16)
+    vc = g.standard_normal((pages, block_size, HKV, D), dtype=np.float32).astype(np.float16)
+    q = g.standard_normal((1, HQ, D), dtype=np.float32).astype(np.float16)
+    bt = g.permutation(pages).astype(np.int32)[None]
+    sl = np.asarray([n], np.int32)
+    oa.paged_decode_attention_ref(q, kc, vc, bt, sl)  # warm-up
+    done, t0 = 0, time.perf_counter()
+    while True:
+        oa.paged_decode_attention_ref(q, kc, vc, bt, sl)
+        done += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    nbytes = decode_call_bytes([n] * done, block_size, HQ, HKV, D, "fp16")
+    desc = (f"{done} x one sequence of {n} tokens (the workload's first length), numpy oracle "
+            f"(numpy BLAS threads = host cores)")
+    return nbytes / dt / 1e9, dt, nbytes, desc
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU algorithm (numpy port) on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    wl = WORKLOADS[args.workload]
+    lens = workload_lens(wl, 0, args.seed)
+    import numpy as np
+    from bpt.roofline import decode_call_bytes
+    from oracle import attention as oa
+    bs = wl["block_size"]
+    g = np.random.Generator(np.random.PCG64(args.seed))
+    # a pool of 2 sequences' pages; each step processes one whole sequence (rotating)
+    sample = [int(x) for x in lens[:2]]
+    pools = []
+    for n in sample:
+        pages = (n + bs - 1) // bs
+        kc = g.standard_normal((pages, bs, HKV, D), dtype=np.float32).astype(np.float16)
+        vc = g.standard_normal((pages, bs, HKV, D), dtype=np.float32).astype(np.float16)
+        q = g.standard_normal((1, HQ, D), dtype=np.float32).astype(np.float16)
+        bt = g.permutation(pages).astype(np.int32)[None]
+        pools.append((q, kc, vc, bt, np.asarray([n], np.int32)))
+    for i in range(args.warmup):
+        oa.paged_decode_attention_ref(*pools[i % len(pools)])
+    t0 = time.perf_counter()
+    nbytes = 0
+    for i in range(args.steps):
+        p = pools[i % len(pools)]
+        oa.paged_decode_attention_ref(*p)
+        nbytes += decode_call_bytes([int(p[4][0])], bs, HQ, HKV, D, "fp16")
+    dt = time.perf_counter() - t0
+    tbps = nbytes / dt / 1e12
+    cores = os.cpu_count()
+    line = {
+        "impl": "reference", "metric": metric_name(wl), "value": tbps, "unit": "TB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_dict(args.workload, wl, args.gpus),
+        "cpu_baseline": {"value": tbps, "unit": "TB/s", "cores": cores, "kind": "port",
+                         "sample": f"each step = one whole sequence of the workload "
+                                   f"({sample} tokens, rotating), numpy oracle"},
+        "e2e": {"value": tbps, "unit": "TB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def metric_name(wl):
+    return (f"achieved HBM TB/s of {wl['fmt']} paged-KV GQA decode "
+            f"(Llama-3-8B layer; % of B200 peak and us/decode step in extra keys)")
+
+
+# ----------------------------------------------------------------------------- bpt arm
+
+def run_bpt(args):
+    import torch
+    import torch.distributed as dist
+    from bpt import decode as dec
+    from bpt.cache import random_paged_workload
+    from bpt.roofline import decode_call_bytes, KIVI_FORMATS
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+
+    wl = WORKLOADS[args.workload]
+    bs = wl["block_size"]
+    lens = workload_lens(wl, rank, args.seed)
+    w = random_paged_workload(lens, HQ, HKV, D, bs, dev, seed=args.seed + rank, spare_blocks=64)
+    q, kc, vc, bt, sl = w["q"], w["k_cache"], w["v_cache"], w["block_table"], w["seq_lens"]
+    B = len(lens)
+    max_blocks = bt.shape[1]
+    sms = dec._sm_count(local)
+    S = dec.effective_splits(B, HKV, bs, max_blocks, None, sms)
+    step_bytes = decode_call_bytes(lens, bs, HQ, HKV, D, wl["fmt"])
+    f = KIVI_FORMATS[wl["fmt"]]
+    kernel_bytes = step_bytes - B * HQ * D * 2  # the split kernel does not write `out`
+    out = torch.empty_like(q)
+    o_part = torch.empty(B, HQ, S, D, dtype=torch.float32, device=dev)
+    lse = torch.empty(B, HQ, S, dtype=torch.float32, device=dev)
+    launches_per_step = 2 if S > 1 else 1
+
+    stream = torch.cuda.current_stream(dev)
+
+    def step(ev_a=None, ev_b=None):
+        if S > 1:
+            if ev_a is not None:
+                ev_a.record(stream)
+            dec.paged_decode_attention_partial(q, kc, vc, bt, sl, num_splits=S, o_part=o_part,
+                                               lse=lse)
+            if ev_b is not None:
+                ev_b.record(stream)
+            dec.merge_partials(o_part, lse, out=out)
+        else:
+            if ev_a is not None:
+                ev_a.record(stream)
+            dec.paged_decode_attention(q, kc, vc, bt, sl, num_splits=1, out=out)
+            if ev_b is not None:
+                ev_b.record(stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    for _ in range(max(args.warmup, 0)):
+        step()
+    torch.cuda.synchronize()
+
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local)
+    barrier()
+    torch.cuda.synchronize()
+    with sampler:
+        t_start.record(stream)
+        for i in range(args.steps):
+            step(*evs[i])
+        t_end.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    elapsed_ms = t_start.elapsed_time(t_end)
+    kern_ms = sum(a.elapsed_time(b) for a, b in evs) / max(args.steps, 1)
+
+    tot = torch.tensor([elapsed_ms, step_bytes * args.steps], dtype=torch.float64, device=dev)
+    if world > 1:
+        t_max = tot[:1].clone()
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+        b_sum = tot[1:].clone()
+        dist.all_reduce(b_sum, op=dist.ReduceOp.SUM)
+        elapsed_max, bytes_all = float(t_max.item()), float(b_sum.item())
+    else:
+        elapsed_max, bytes_all = elapsed_ms, float(step_bytes * args.steps)
+    value_tbps = bytes_all / (elapsed_max * 1e-3) / 1e12
+
+    # ---- e2e through the public API, host buffers, copies inside the timed region
+    e2e = None
+    if not args.no_e2e:
+        q_h = q.cpu().pin_memory()
+        bt_h = bt.cpu().pin_memory()
+        sl_h = sl.cpu().pin_memory()
+        out_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+        ws = torch.empty(dec.workspace_bytes(B, HQ, D, S), dtype=torch.uint8, device=dev)
+
+        def e2e_step():
+            q.copy_(q_h, non_blocking=True)
+            bt.copy_(bt_h, non_blocking=True)
+            sl.copy_(sl_h, non_blocking=True)
+            dec.paged_decode_attention(q, kc, vc, bt, sl, out=out, workspace=ws)
+            out_h.copy_(out, non_blocking=True)
+
+        for _ in range(max(args.warmup, 1)):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+        e2e = {"value": bytes_all / (float(e_ms.item()) * 1e-3) / 1e12, "unit": "TB/s",
+               "h2d_bytes_per_step": q.nbytes + bt.nbytes + sl.nbytes,
+               "d2h_bytes_per_step": out.nbytes,
+               "ms_per_step": float(e_ms.item()) / args.steps,
+               "note": "public API bpt.paged_decode_attention; KV cache resident in HBM"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        gbps, secs, nbytes, desc = cpu_oracle_sample(lens, bs, args.seed, args.cpu_seconds)
+        cpu = {"value": gbps / 1e3, "unit": "TB/s", "cores": os.cpu_count(), "kind": "port",
+               "sample": desc, "seconds": round(secs, 2)}
+
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+
+    peak, peak_src = measured_peaks()
+    achieved_gbs = kernel_bytes / (kern_ms * 1e-3) / 1e9
+    traffic, traffic_note = ncu_traffic(args.workload)
+    ms_per_step = elapsed_max / args.steps
+    line = {
+        "metric": metric_name(wl),
+        "value": value_tbps, "unit": "TB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": value_tbps / REFERENCE_PUBLISHED_TBPS,
+        "vs_baseline_ref": "reference's best published Triton FP16 figure, 1.638 TB/s "
+                           "(A100-80GB, B=32 ctx=16k, docs/NOTES.md:99)",
+        "dtype": "f16", "data": "synthetic (seeded N(0,1) fp16 q/K/V, random block tables)",
+        "config": config_dict(args.workload, wl, world),
+        "pct_of_b200_spec_peak": 100.0 * value_tbps * 1e3 / (B200_SPEC_GBS * world),
+        "us_per_decode_step": {"one_layer": ms_per_step * 1e3,
+                               "llama3_8b_32_layers": ms_per_step * 1e3 * 32},
+        "splits": S,
+        "roofline": {"bound": "hbm", "kernel": "split_kv_fp16_kernel",
+                     "achieved": achieved_gbs, "peak": peak, "unit": "GB/s",
+                     "frac": achieved_gbs / peak, "peak_source": peak_src,
+                     "traffic": traffic, "traffic_note": traffic_note,
+                     "algorithmic_bytes_per_launch": kernel_bytes,
+                     "kernel_ms_per_launch": kern_ms},
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "gpu_launches": args.steps * launches_per_step,
+        "clocks": sampler.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_bpt(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,112 @@
+/*
+ * bpt — B200-native paged-KV GQA decode attention: the C ABI.
+ *
+ * Every entry point takes plain device pointers, element strides and sizes, a caller-owned
+ * device workspace and a cudaStream_t passed as void*. Nothing here allocates, synchronises
+ * the host or reads device memory from the host, so every call can be enqueued inside a
+ * CUDA graph capture. Return value: 0 = success, negative = bpt_status (see below);
+ * bpt_status_string() turns it into text.
+ *
+ * Layouts (vLLM-style paged cache, the reference's layout, src/bpt/reference.py:3-9):
+ *   q            [B, Hq, D]                        fp16, inner stride 1
+ *   k/v cache    [num_blocks, block_size, Hkv, D]  inner stride 1, other strides free
+ *   block_table  [B, max_blocks] int32             logical page -> physical block
+ *   seq_lens     [B] int32                         valid tokens per sequence (0 allowed)
+ *   out          [B, Hq, D] fp16
+ */
+#ifndef BPT_H_
+#define BPT_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum bpt_status {
+  BPT_OK = 0,
+  BPT_ERR_INVALID_ARGUMENT = -1,  /* null pointer, negative size, Hq % Hkv != 0, ... */
+  BPT_ERR_UNSUPPORTED_SHAPE = -2, /* head_dim / group / block_size outside the built set */
+  BPT_ERR_WORKSPACE_TOO_SMALL = -3,
+  BPT_ERR_LAUNCH = -4,            /* CUDA launch or runtime error */
+  BPT_ERR_TENSOR_MAP = -5,        /* cuTensorMapEncodeTiled rejected the cache view */
+  BPT_ERR_ALIGNMENT = -6,         /* pointer / stride not 16-byte aligned */
+  BPT_ERR_DRIVER = -7,            /* driver entry point unavailable */
+  BPT_ERR_DEVICE_CHECK = -8,      /* device-side check tripped (see bpt_device_flags) */
+  BPT_ERR_NO_DEVICE = -9
+};
+
+/* Device-side check flags, OR-ed into the first 4 bytes of the workspace by the kernels.
+ * Reading them needs a device->host copy, so the host library never does it on its own;
+ * the Python layer does it only in checked mode (BPT_CHECKS=1). */
+enum bpt_device_flags {
+  BPT_DEV_BAD_BLOCK_ID = 1,    /* block_table entry outside [0, num_blocks) */
+  BPT_DEV_SEQ_TOO_LONG = 2,    /* seq_len > max_blocks * block_size (clamped) */
+  BPT_DEV_WAIT_TIMEOUT = 4,    /* a pipeline wait gave up after its time budget */
+  BPT_DEV_NEG_SEQ_LEN = 8      /* seq_len < 0 (treated as 0) */
+};
+
+const char* bpt_status_string(int status);
+int bpt_version(void);
+
+/* Number of KV splits the heuristic picks. Replaces choose_num_splits
+ * (src/bpt/triton_fp16.py:175-180); B200 tuning (148 SMs, 64-token chunks). */
+int bpt_plan_splits(int batch, int kv_heads, int block_size, int max_blocks, int sm_count);
+
+/* Split count a decode call actually uses for a requested num_splits (<= 0 = heuristic),
+ * mirroring the clamping of src/bpt/triton_fp16.py:208-217. */
+int bpt_effective_splits(int batch, int kv_heads, int block_size, int max_blocks,
+                         int num_splits, int sm_count);
+
+/* Workspace bytes a decode call with this many effective splits needs. */
+size_t bpt_decode_workspace_bytes(int batch, int q_heads, int head_dim, int splits);
+
+/* FP16 paged decode: replaces paged_decode_attention_triton
+ * (src/bpt/triton_fp16.py:183-247) and its kernels _split_kernel (:83-144),
+ * _paged_decode_kernel (:25-80) and _merge_kernel (:147-163).
+ * Strides are in elements. scale <= 0 selects 1/sqrt(head_dim) (triton_fp16.py:203-204).
+ * num_splits: <= 0 heuristic, 1 single pass, n n-way split (triton_fp16.py:192).
+ * sm_count: SMs of the target device, used only by the heuristic (<= 0: query it). */
+int bpt_decode_fp16(const void* q, int64_t q_sb, int64_t q_sh,
+                    const void* k_cache, int64_t k_sb, int64_t k_st, int64_t k_sh,
+                    const void* v_cache, int64_t v_sb, int64_t v_st, int64_t v_sh,
+                    int64_t num_blocks,
+                    const int32_t* block_table, int64_t bt_sb,
+                    const int32_t* seq_lens,
+                    void* out, int64_t o_sb, int64_t o_sh,
+                    int batch, int q_heads, int kv_heads, int head_dim,
+                    int block_size, int max_blocks,
+                    float scale, int num_splits, int sm_count,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* Stage 1 alone: the split kernel (src/bpt/triton_fp16.py:83-144) with exactly `splits`
+ * splits, writing normalised fp32 partial outputs o_part [B, Hq, splits, D] and their
+ * log2-sum-exp lse [B, Hq, splits] (log2 units: lse2 = ln-sum-exp * log2(e); -inf for an
+ * empty split). Used for sequence sharding across GPUs, where each rank's states are merged
+ * after an all-gather. status (nullable) receives bpt_device_flags. */
+int bpt_decode_fp16_partial(const void* q, int64_t q_sb, int64_t q_sh,
+                            const void* k_cache, int64_t k_sb, int64_t k_st, int64_t k_sh,
+                            const void* v_cache, int64_t v_sb, int64_t v_st, int64_t v_sh,
+                            int64_t num_blocks,
+                            const int32_t* block_table, int64_t bt_sb,
+                            const int32_t* seq_lens,
+                            int batch, int q_heads, int kv_heads, int head_dim,
+                            int block_size, int max_blocks, float scale, int splits,
+                            float* o_part, float* lse, unsigned* status, void* stream);
+
+/* Stage 2: merge `splits` partial states per (b, q head) into fp16 out [B, Hq, D]
+ * (replaces _merge_kernel, src/bpt/triton_fp16.py:147-163). */
+int bpt_merge_partials(const float* o_part, const float* lse, int batch, int q_heads,
+                       int head_dim, int splits, void* out, int64_t o_sb, int64_t o_sh,
+                       void* stream);
+
+/* Stage 2 keeping fp32 state: merged o [B, Hq, D] (contiguous) and lse [B, Hq] (log2). */
+int bpt_merge_states(const float* o_part, const float* lse, int batch, int q_heads,
+                     int head_dim, int splits, float* o_out, float* lse_out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BPT_H_ */

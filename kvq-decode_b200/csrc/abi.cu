@@ -1,0 +1,129 @@
+// C-ABI utilities: status strings, split planner, workspace sizing, tensor-map encoding.
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "decode_common.h"
+
+namespace bpt {
+
+namespace {
+
+constexpr int kChunkTokens = 64;    // tokens per pipeline stage of the decode kernels
+constexpr int kResidentCtas = 2;    // decode CTAs resident per SM (shared-memory bound)
+constexpr int kMinChunksPerSplit = 4;
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+}  // namespace
+
+int device_sm_count() {
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return 148;
+  return sms;
+}
+
+WorkspaceView workspace_view(void* ws, int batch, int q_heads, int head_dim, int splits) {
+  (void)head_dim;
+  char* base = static_cast<char*>(ws);
+  WorkspaceView v;
+  v.status = reinterpret_cast<unsigned*>(base);
+  v.lse = reinterpret_cast<float*>(base + 256);
+  const size_t lse_bytes = align256(size_t(batch) * q_heads * splits * sizeof(float));
+  v.o_part = reinterpret_cast<float*>(base + 256 + lse_bytes);
+  return v;
+}
+
+int encode_kv_map(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes,
+                  int inner, int kv_heads, int block_size, int64_t num_blocks, int64_t s_head,
+                  int64_t s_tok, int64_t s_blk, int box_inner, int box_rows,
+                  int* token_is_dim1) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return BPT_ERR_DRIVER;
+  if (reinterpret_cast<uintptr_t>(base) & 15) return BPT_ERR_ALIGNMENT;
+  if (num_blocks <= 0) num_blocks = 1;  // an empty cache is never read (no valid token)
+  const int64_t sh = s_head * elem_bytes, st = s_tok * elem_bytes, sb = s_blk * elem_bytes;
+  if ((sh % 16) || (st % 16) || (sb % 16)) return BPT_ERR_ALIGNMENT;
+  const bool tok1 = st < sh;  // head-major page ([block, head, token, inner])
+  *token_is_dim1 = tok1 ? 1 : 0;
+  cuuint64_t dims[4] = {cuuint64_t(inner), cuuint64_t(tok1 ? block_size : kv_heads),
+                        cuuint64_t(tok1 ? kv_heads : block_size), cuuint64_t(num_blocks)};
+  cuuint64_t strides[3] = {cuuint64_t(tok1 ? st : sh), cuuint64_t(tok1 ? sh : st),
+                           cuuint64_t(sb)};
+  cuuint32_t box[4] = {cuuint32_t(box_inner), cuuint32_t(tok1 ? box_rows : 1),
+                       cuuint32_t(tok1 ? 1 : box_rows), 1u};
+  cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  CUresult r = enc(map, dtype, 4, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? BPT_OK : BPT_ERR_TENSOR_MAP;
+}
+
+}  // namespace bpt
+
+using namespace bpt;
+
+extern "C" const char* bpt_status_string(int status) {
+  switch (status) {
+    case BPT_OK: return "ok";
+    case BPT_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case BPT_ERR_UNSUPPORTED_SHAPE: return "unsupported shape (head_dim/group/block_size)";
+    case BPT_ERR_WORKSPACE_TOO_SMALL: return "workspace too small";
+    case BPT_ERR_LAUNCH: return "CUDA launch error";
+    case BPT_ERR_TENSOR_MAP: return "tensor map encoding rejected the cache view";
+    case BPT_ERR_ALIGNMENT: return "pointer or stride not 16-byte aligned";
+    case BPT_ERR_DRIVER: return "CUDA driver entry point unavailable";
+    case BPT_ERR_DEVICE_CHECK: return "device-side check failed";
+    case BPT_ERR_NO_DEVICE: return "no CUDA device";
+    default: return "unknown status";
+  }
+}
+
+extern "C" int bpt_version(void) { return 100; }
+
+extern "C" int bpt_plan_splits(int batch, int kv_heads, int block_size, int max_blocks,
+                               int sm_count) {
+  if (sm_count <= 0) sm_count = device_sm_count();
+  const int64_t units = (int64_t(max_blocks) * block_size + kChunkTokens - 1) / kChunkTokens;
+  const int64_t work = int64_t(batch > 0 ? batch : 1) * (kv_heads > 0 ? kv_heads : 1);
+  const int64_t target = int64_t(sm_count) * kResidentCtas * 2;  // two waves of CTAs
+  int64_t want = (target + work - 1) / work;
+  int64_t cap = units / kMinChunksPerSplit;
+  if (cap < 1) cap = 1;
+  if (want > cap) want = cap;
+  if (want < 1) want = 1;
+  return int(want);
+}
+
+extern "C" int bpt_effective_splits(int batch, int kv_heads, int block_size, int max_blocks,
+                                    int num_splits, int sm_count) {
+  int s = num_splits > 0 ? num_splits
+                         : bpt_plan_splits(batch, kv_heads, block_size, max_blocks, sm_count);
+  const int64_t units = (int64_t(max_blocks) * block_size + kChunkTokens - 1) / kChunkTokens;
+  if (s > units) s = int(units);
+  if (s < 1) s = 1;
+  return s;
+}
+
+extern "C" size_t bpt_decode_workspace_bytes(int batch, int q_heads, int head_dim, int splits) {
+  if (batch <= 0 || q_heads <= 0 || head_dim <= 0 || splits <= 0) return 256;
+  const size_t rows = size_t(batch) * q_heads * splits;
+  return 256 + align256(rows * sizeof(float)) + rows * head_dim * sizeof(float);
+}

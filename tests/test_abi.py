@@ -1,0 +1,72 @@
+"""The C-ABI library loads on a CPU-only machine and exports every declared entry point;
+host-only entry points (planner, workspace sizing, status strings) behave."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from bpt import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    names = []
+    for fn in sorted(os.listdir(os.path.join(ROOT, "include"))):
+        if not fn.endswith(".h"):
+            continue
+        text = open(os.path.join(ROOT, "include", fn)).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        names += re.findall(r"\b(bpt_[a-z0-9_]+)\s*\(", text)
+    return sorted(set(names))
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    assert "bpt_decode_fp16" in names and "bpt_plan_splits" in names
+
+
+@pytest.mark.parametrize("name", declared_functions())
+def test_library_exports_symbol(name):
+    lib = ctypes.CDLL(_lib.LIB_PATH)
+    assert hasattr(lib, name), f"{name} declared in include/ but not exported"
+
+
+def test_status_strings():
+    assert _lib.status_string(0) == "ok"
+    assert "workspace" in _lib.status_string(-3)
+    assert _lib.status_string(12345) == "unknown status"
+
+
+def test_planner_fills_b200():
+    from bpt.decode import choose_num_splits, effective_splits
+    # B=1, 64k tokens, bs=16: enough CTAs for 148 SMs
+    s = choose_num_splits(1, 8, 16, 4096, 148)
+    assert 8 * s >= 2 * 148
+    # large batch: no split needed
+    assert choose_num_splits(64, 8, 16, 4096, 148) <= 2
+    # short context caps the split count (>= 4 chunks of 64 tokens per split)
+    assert choose_num_splits(1, 8, 16, 16, 148) == 1
+    # explicit requests are clamped to the chunk count
+    assert effective_splits(2, 8, 16, 4, 7, 148) == 1
+    assert effective_splits(2, 8, 16, 512, 7, 148) == 7
+    assert effective_splits(2, 8, 16, 512, 1, 148) == 1
+
+
+def test_workspace_bytes_monotone():
+    from bpt.decode import workspace_bytes
+    a = workspace_bytes(2, 32, 128, 1)
+    b = workspace_bytes(2, 32, 128, 8)
+    assert b > a >= 256
+    assert b >= 256 + 2 * 32 * 8 * 128 * 4
+
+
+def test_compute_entry_rejects_bad_arguments_without_gpu():
+    lib = _lib.lib()
+    rc = lib.bpt_decode_fp16(None, 0, 0, None, 0, 0, 0, None, 0, 0, 0, 0, None, 0, None, None,
+                             0, 0, 1, 32, 7, 128, 16, 1, 0.0, 0, 148, None, 0, None)
+    assert rc == _lib.ERR_INVALID_ARGUMENT  # Hq % Hkv != 0
+    rc = lib.bpt_decode_fp16(None, 0, 0, None, 0, 0, 0, None, 0, 0, 0, 0, None, 0, None, None,
+                             0, 0, 0, 32, 8, 128, 16, 1, 0.0, 0, 148, None, 0, None)
+    assert rc == 0  # empty batch is a no-op
