@@ -194,3 +194,24 @@ def test_full_size_batch_against_torch_fp32(B, ctx):
         out = paged_decode_attention(w["q"], w["k_cache"], w["v_cache"], w["block_table"],
                                      w["seq_lens"], num_splits=ns)
         assert_close(out.float().cpu().numpy(), ref.cpu().numpy(), what=f"B={B} ctx={ctx}")
+
+
+@pytest.mark.parametrize("splits", [1, 4, 9])
+def test_partial_states_and_merges(splits):
+    """bpt_decode_fp16_partial + bpt_merge_states give the oracle's per-sequence state
+    (o, lse); lse is reported in log2 units."""
+    from bpt.decode import merge_partials, merge_states, paged_decode_attention_partial
+    from oracle import attention as oa
+    name = "fp16_h32_8_d128_bs16_l4096-1000-17-2049"
+    spec, c = _case(name)
+    q, kc, vc, bt, sl = _to_gpu(c)
+    o_part, lse = paged_decode_attention_partial(q, kc, vc, bt, sl, num_splits=splits)
+    assert o_part.shape[2] == splits
+    out = merge_partials(o_part, lse)
+    assert_close(out.cpu().numpy(), golden_arrays()[name + "/out"], what="merge_partials")
+    o, l2 = merge_states(o_part, lse)
+    lens = c["seq_lens"]
+    o_ref, lse_ref = oa.paged_decode_attention_partial(
+        c["q"], c["k_cache"], c["v_cache"], c["block_table"], lens, np.zeros_like(lens), lens)
+    assert np.abs(o.cpu().numpy() - o_ref).max() < 1e-4
+    assert np.abs(l2.cpu().numpy() - lse_ref * np.log2(np.e)).max() < 1e-4
