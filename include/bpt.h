@@ -105,6 +105,30 @@ int bpt_merge_partials(const float* o_part, const float* lse, int batch, int q_h
 int bpt_merge_states(const float* o_part, const float* lse, int batch, int q_heads,
                      int head_dim, int splits, float* o_out, float* lse_out, void* stream);
 
+/* Size of the fixed scratch array behind bpt_decode_fp16_noalloc, per GPU. */
+#define BPT_NOALLOC_SCRATCH_BYTES (8u * 1024u * 1024u)
+
+/* bpt_decode_fp16 without a workspace argument, for callers that cannot allocate device
+ * memory when they call (an engine that owns all device memory after start-up, a plugin
+ * handed only its input and output buffers, code running where allocation is not allowed).
+ * No counterpart in the reference. The split-KV partial states live in a fixed
+ * BPT_NOALLOC_SCRATCH_BYTES array inside the library, reserved on each GPU that loads it until
+ * the process exits; a call needing more (B * Hq * splits * (head_dim + 1) * 4 bytes, rounded)
+ * returns BPT_ERR_WORKSPACE_TOO_SMALL without launching. The first call on a device looks up
+ * that device's array address (cudaGetSymbolAddress, with the device current); make it before
+ * any stream capture. All calls share the array: calls whose kernels overlap on the GPU race.
+ * It allocates nothing and records no device-check flags. Other arguments as bpt_decode_fp16. */
+int bpt_decode_fp16_noalloc(const void* q, int64_t q_sb, int64_t q_sh,
+                            const void* k_cache, int64_t k_sb, int64_t k_st, int64_t k_sh,
+                            const void* v_cache, int64_t v_sb, int64_t v_st, int64_t v_sh,
+                            int64_t num_blocks,
+                            const int32_t* block_table, int64_t bt_sb,
+                            const int32_t* seq_lens,
+                            void* out, int64_t o_sb, int64_t o_sh,
+                            int batch, int q_heads, int kv_heads, int head_dim,
+                            int block_size, int max_blocks,
+                            float scale, int num_splits, int sm_count, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

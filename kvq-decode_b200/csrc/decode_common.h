@@ -51,6 +51,15 @@ int launch_merge(const float* o_part, const float* lse, int batch, int q_heads, 
                  int D, __half* out16, int64_t o_sb, int64_t o_sh, float* o32, float* lse32,
                  cudaStream_t st);
 
+// Validate, encode the tensor maps and launch the FP16 split kernel (decode_fp16.cu).
+int run_split_fp16(const void* q, int64_t q_sb, int64_t q_sh, const void* k_cache, int64_t k_sb,
+                   int64_t k_st, int64_t k_sh, const void* v_cache, int64_t v_sb, int64_t v_st,
+                   int64_t v_sh, int64_t num_blocks, const int32_t* block_table, int64_t bt_sb,
+                   const int32_t* seq_lens, void* out, int64_t o_sb, int64_t o_sh, int batch,
+                   int q_heads, int kv_heads, int head_dim, int block_size, int max_blocks,
+                   float scale, int splits, int final_out, float* o_part, float* lse,
+                   unsigned* status, cudaStream_t st);
+
 int device_sm_count();
 
 }  // namespace bpt
