@@ -10,9 +10,10 @@ planner (CTAs resident per SM, minimum tokens per split).
 """
 from .decode import _sm_count, choose_num_splits, paged_decode_attention
 
-# reference: src/bpt/triton_fp16.py:166-167 (values are the B200 planner's)
-TARGET_PROGRAMS_PER_SM = 4     # 2 resident CTAs/SM x 2 waves
-MIN_TOKENS_PER_SPLIT = 256     # 4 chunks of 64 tokens
+# reference: src/bpt/triton_fp16.py:166-167 (values are the B200 planner's: one wave of
+# 4 resident CTAs per SM when >= 4 splits fit, else ~8 waves; >= 2 chunks of 32 tokens)
+TARGET_PROGRAMS_PER_SM = 4
+MIN_TOKENS_PER_SPLIT = 64
 
 paged_decode_attention_triton = paged_decode_attention
 

@@ -10,9 +10,11 @@ namespace bpt {
 
 namespace {
 
-constexpr int kChunkTokens = 64;    // tokens per pipeline stage of the decode kernels
-constexpr int kResidentCtas = 2;    // decode CTAs resident per SM (shared-memory bound)
-constexpr int kMinChunksPerSplit = 4;
+constexpr int kChunkTokens = 32;    // tokens per pipeline stage of the decode kernels
+constexpr int kResidentCtas = 4;    // decode CTAs resident per SM
+constexpr int kMinChunksPerSplit = 2;
+constexpr int kMinSingleWaveSplits = 4;
+constexpr int kWaves = 8;
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
@@ -54,7 +56,7 @@ WorkspaceView workspace_view(void* ws, int batch, int q_heads, int head_dim, int
 int encode_kv_map(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes,
                   int inner, int kv_heads, int block_size, int64_t num_blocks, int64_t s_head,
                   int64_t s_tok, int64_t s_blk, int box_inner, int box_rows,
-                  int* token_is_dim1) {
+                  int* token_is_dim1, int swizzle_bytes) {
   auto enc = tensor_map_encoder();
   if (!enc) return BPT_ERR_DRIVER;
   if (reinterpret_cast<uintptr_t>(base) & 15) return BPT_ERR_ALIGNMENT;
@@ -70,8 +72,12 @@ int encode_kv_map(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
   cuuint32_t box[4] = {cuuint32_t(box_inner), cuuint32_t(tok1 ? box_rows : 1),
                        cuuint32_t(tok1 ? 1 : box_rows), 1u};
   cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_NONE;
+  if (swizzle_bytes == 128) sw = CU_TENSOR_MAP_SWIZZLE_128B;
+  else if (swizzle_bytes == 64) sw = CU_TENSOR_MAP_SWIZZLE_64B;
+  else if (swizzle_bytes == 32) sw = CU_TENSOR_MAP_SWIZZLE_32B;
   CUresult r = enc(map, dtype, 4, const_cast<void*>(base), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? BPT_OK : BPT_ERR_TENSOR_MAP;
 }
@@ -100,11 +106,16 @@ extern "C" int bpt_version(void) { return 100; }
 
 extern "C" int bpt_plan_splits(int batch, int kv_heads, int block_size, int max_blocks,
                                int sm_count) {
+  // One CTA per (sequence, kv head, split); kResidentCtas of them fit on an SM at once.
+  // If at least 4 splits still fit in ONE wave, use exactly that many (every CTA starts
+  // together, no tail); otherwise aim for ~8 waves of shorter CTAs so the ragged tail is
+  // small. Never split below 2 chunks per split.
   if (sm_count <= 0) sm_count = device_sm_count();
   const int64_t units = (int64_t(max_blocks) * block_size + kChunkTokens - 1) / kChunkTokens;
   const int64_t work = int64_t(batch > 0 ? batch : 1) * (kv_heads > 0 ? kv_heads : 1);
-  const int64_t target = int64_t(sm_count) * kResidentCtas * 2;  // two waves of CTAs
-  int64_t want = (target + work - 1) / work;
+  const int64_t resident = int64_t(sm_count) * kResidentCtas;
+  int64_t want = resident / work;
+  if (want < kMinSingleWaveSplits) want = (kWaves * resident + work - 1) / work;
   int64_t cap = units / kMinChunksPerSplit;
   if (cap < 1) cap = 1;
   if (want > cap) want = cap;

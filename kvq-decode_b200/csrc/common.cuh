@@ -97,6 +97,20 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// ----------------------------------------------------------------------------- PDL
+
+// Let a programmatically dependent grid (the split merge) start launching; it still waits
+// for this grid's completion in pdl_wait() before reading anything this grid wrote.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Wait until the preceding grid in the stream has completed and its writes are visible
+// (a no-op when the grid was not launched as a programmatic dependent).
+__device__ __forceinline__ void pdl_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // ----------------------------------------------------------------------------- misc
 
 __device__ __forceinline__ void named_barrier_sync(int id, int threads) {

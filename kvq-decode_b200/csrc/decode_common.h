@@ -40,16 +40,20 @@ WorkspaceView workspace_view(void* ws, int batch, int q_heads, int head_dim, int
 // 4-D tiled tensor map over a paged cache [num_blocks, block_size, Hkv, inner] whose inner
 // dimension is contiguous; strides in elements. The two middle dimensions are ordered by
 // stride; *token_is_dim1 tells the kernel which coordinate is which. The box is
-// {box_inner, 1 head, box_rows tokens, 1 block}.
+// {box_inner, 1 head, box_rows tokens, 1 block}. swizzle_bytes: 0 (none), 32, 64 or 128 (the
+// box's inner extent in bytes must not exceed it); a swizzled box lands in shared memory with
+// 16-byte chunk c of row r stored at chunk c ^ (r % (swizzle_bytes / 16)).
 int encode_kv_map(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes,
                   int inner, int kv_heads, int block_size, int64_t num_blocks, int64_t s_head,
-                  int64_t s_tok, int64_t s_blk, int box_inner, int box_rows, int* token_is_dim1);
+                  int64_t s_tok, int64_t s_blk, int box_inner, int box_rows, int* token_is_dim1,
+                  int swizzle_bytes = 0);
 
 // Merge `splits` partial states per (b, q head). Exactly one of out16 (fp16 [B, Hq, D] with
-// strides o_sb/o_sh) or (o32 [B, Hq, D] contiguous fp32 + lse32 [B, Hq]) is written.
+// strides o_sb/o_sh) or (o32 [B, Hq, D] contiguous fp32 + lse32 [B, Hq]) is written. pdl:
+// launch as a programmatic dependent of the split kernel just enqueued on the same stream.
 int launch_merge(const float* o_part, const float* lse, int batch, int q_heads, int splits,
                  int D, __half* out16, int64_t o_sb, int64_t o_sh, float* o32, float* lse32,
-                 cudaStream_t st);
+                 cudaStream_t st, bool pdl);
 
 // Validate, encode the tensor maps and launch the FP16 split kernel (decode_fp16.cu).
 int run_split_fp16(const void* q, int64_t q_sb, int64_t q_sh, const void* k_cache, int64_t k_sb,

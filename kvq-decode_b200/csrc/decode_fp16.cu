@@ -24,6 +24,7 @@
 
 #include "common.cuh"
 #include "decode_common.h"
+#include "mma_decode.cuh"
 
 namespace bpt {
 
@@ -212,6 +213,7 @@ split_kv_fp16_kernel(const __grid_constant__ CUtensorMap tmK,
       ++issued;
     }
     (void)ok;
+    pdl_launch_dependents();
     // Drain: never leave the CTA with a bulk copy still writing its shared memory.
     if (lane == 0) {
       for (int c = max(0, issued - G::STAGES); c < issued; ++c)
@@ -344,6 +346,7 @@ split_kv_fp16_kernel(const __grid_constant__ CUtensorMap tmK,
     if (lane == 0) mbar_arrive(&empty[stage]);
   }
 
+  pdl_launch_dependents();
   // Reduce over the token groups of the warp.
 #pragma unroll
   for (int off = G::LPT; off < 32; off <<= 1) {
@@ -408,6 +411,7 @@ merge_splits_kernel(const float* __restrict__ o_part, const float* __restrict__ 
   const int64_t row0 = (int64_t(b) * q_heads + hq) * splits;
   const float* l = lse + row0;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  pdl_wait();
 
   float m = kNegInf;
   for (int s = tid; s < splits; s += blockDim.x) m = fmaxf(m, l[s]);
@@ -471,23 +475,74 @@ int dispatch_group(int gp, const CUtensorMap& tk, const CUtensorMap& tv, const D
   }
 }
 
+
+#ifndef BPT_FP16_NCW
+#define BPT_FP16_NCW 2      // consumer warps per CTA (chunk = 16 * NCW tokens)
+#endif
+#ifndef BPT_FP16_STAGES
+#define BPT_FP16_STAGES 3   // shared-memory ring depth
+#endif
+#ifndef BPT_FP16_MINB
+#define BPT_FP16_MINB 4     // CTAs per SM the register budget is sized for
+#endif
+
+// Tensor-core kernel configuration for head_dim D. Many resident CTAs (independent TMA
+// streams) per SM matter more than a deep ring: for D <= 128 a CTA is 2 consumer warps + 1
+// producer warp streaming 32-token chunks through a 3-stage ring (48 KB at D=128), 4 CTAs
+// per SM. Measured on B200 against 2-4 consumer warps, 2-4 stages, 2-6 CTAs/SM.
+template <int D>
+struct Fp16Tc {
+  static constexpr int NCW = D >= 256 ? 4 : BPT_FP16_NCW;
+  static constexpr int STAGES = D >= 256 ? 2 : BPT_FP16_STAGES;
+  static constexpr int MINB = D >= 256 ? 1 : BPT_FP16_MINB;
+  static constexpr int CHUNK = 16 * NCW;
+};
+
+template <int D>
+int launch_split_mma(bool g8, const CUtensorMap& tk, const CUtensorMap& tv,
+                     const DecodeParams& p, cudaStream_t st) {
+  using T = Fp16Tc<D>;
+  return g8 ? mma::launch<D, T::NCW, T::STAGES, T::MINB, true>(tk, tv, p, st)
+            : mma::launch<D, T::NCW, T::STAGES, T::MINB, false>(tk, tv, p, st);
+}
+
+int tc_chunk_tokens(int head_dim) {
+  switch (head_dim) {
+    case 64: return Fp16Tc<64>::CHUNK;
+    case 128: return Fp16Tc<128>::CHUNK;
+    case 256: return Fp16Tc<256>::CHUNK;
+    default: return kChunk;
+  }
+}
+
 }  // namespace
 
 int launch_merge(const float* o_part, const float* lse, int batch, int q_heads, int splits,
                  int D, __half* out16, int64_t o_sb, int64_t o_sh, float* o32, float* lse32,
-                 cudaStream_t st) {
+                 cudaStream_t st, bool pdl) {
   if (batch <= 0) return BPT_OK;
-  dim3 grid(q_heads, batch);
   const size_t sm = size_t(splits) * sizeof(float);
   if (sm > 48 * 1024) return BPT_ERR_UNSUPPORTED_SHAPE;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(q_heads, batch);
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = sm;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t e;
   if (out16) {
-    merge_splits_kernel<true><<<grid, 128, sm, st>>>(o_part, lse, q_heads, splits, D, out16,
-                                                     o_sb, o_sh, nullptr, nullptr);
+    e = cudaLaunchKernelEx(&cfg, merge_splits_kernel<true>, o_part, lse, q_heads, splits, D,
+                           out16, o_sb, o_sh, static_cast<float*>(nullptr),
+                           static_cast<float*>(nullptr));
   } else {
-    merge_splits_kernel<false><<<grid, 128, sm, st>>>(o_part, lse, q_heads, splits, D, nullptr,
-                                                      0, 0, o32, lse32);
+    e = cudaLaunchKernelEx(&cfg, merge_splits_kernel<false>, o_part, lse, q_heads, splits, D,
+                           static_cast<__half*>(nullptr), int64_t(0), int64_t(0), o32, lse32);
   }
-  return cudaGetLastError() == cudaSuccess ? BPT_OK : BPT_ERR_LAUNCH;
+  return e == cudaSuccess ? BPT_OK : BPT_ERR_LAUNCH;
 }
 
 // Validate, encode the tensor maps and launch the split kernel. `final_out` selects the
@@ -518,13 +573,21 @@ int run_split_fp16(const void* q, int64_t q_sb, int64_t q_sh, const void* k_cach
   if (((q_sb * 2) % 16) || ((q_sh * 2) % 16)) return BPT_ERR_ALIGNMENT;
 
   DecodeParams p{};
-  const int box_rows = block_size < 64 ? block_size : 64;
+  // head_dim a multiple of 64: tensor-core kernel over 64-column swizzled boxes;
+  // head_dim 16 / 32: CUDA-core kernel over whole rows.
+  const bool mma_path = head_dim % 64 == 0;
+  const int chunk = mma_path ? tc_chunk_tokens(head_dim) : kChunk;
+  const int box_rows = block_size < chunk ? block_size : chunk;
+  const int box_inner = mma_path ? 64 : head_dim;
+  const int swizzle = mma_path ? 128 : 0;
   CUtensorMap tk, tv;
   int rc = encode_kv_map(&tk, k_cache, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, head_dim, kv_heads,
-                         block_size, num_blocks, k_sh, k_st, k_sb, head_dim, box_rows, &p.k_c1);
+                         block_size, num_blocks, k_sh, k_st, k_sb, box_inner, box_rows, &p.k_c1,
+                         swizzle);
   if (rc) return rc;
   rc = encode_kv_map(&tv, v_cache, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, head_dim, kv_heads,
-                     block_size, num_blocks, v_sh, v_st, v_sb, head_dim, box_rows, &p.v_c1);
+                     block_size, num_blocks, v_sh, v_st, v_sb, box_inner, box_rows, &p.v_c1,
+                     swizzle);
   if (rc) return rc;
   p.q = static_cast<const __half*>(q);
   p.q_sb = q_sb;
@@ -553,9 +616,9 @@ int run_split_fp16(const void* q, int64_t q_sb, int64_t q_sh, const void* k_cach
   switch (head_dim) {
     case 16: rc = dispatch_group<16>(gp, tk, tv, p, st); break;
     case 32: rc = dispatch_group<32>(gp, tk, tv, p, st); break;
-    case 64: rc = dispatch_group<64>(gp, tk, tv, p, st); break;
-    case 128: rc = dispatch_group<128>(gp, tk, tv, p, st); break;
-    case 256: rc = dispatch_group<256>(gp, tk, tv, p, st); break;
+    case 64: rc = launch_split_mma<64>(gp > 4, tk, tv, p, st); break;
+    case 128: rc = launch_split_mma<128>(gp > 4, tk, tv, p, st); break;
+    case 256: rc = launch_split_mma<256>(gp > 4, tk, tv, p, st); break;
     default: rc = BPT_ERR_UNSUPPORTED_SHAPE;
   }
   if (rc) return rc;
@@ -593,7 +656,7 @@ extern "C" int bpt_decode_fp16(const void* q, int64_t q_sb, int64_t q_sh, const 
                           ws.o_part, ws.lse, ws.status, st);
   if (rc || S == 1) return rc;
   return launch_merge(ws.o_part, ws.lse, batch, q_heads, S, head_dim,
-                      static_cast<__half*>(out), o_sb, o_sh, nullptr, nullptr, st);
+                      static_cast<__half*>(out), o_sb, o_sh, nullptr, nullptr, st, true);
 }
 
 extern "C" int bpt_decode_fp16_partial(const void* q, int64_t q_sb, int64_t q_sh,
@@ -618,7 +681,7 @@ extern "C" int bpt_merge_partials(const float* o_part, const float* lse, int bat
   if (batch == 0) return BPT_OK;
   if (!o_part || !lse || !out) return BPT_ERR_INVALID_ARGUMENT;
   return launch_merge(o_part, lse, batch, q_heads, splits, head_dim, static_cast<__half*>(out),
-                      o_sb, o_sh, nullptr, nullptr, static_cast<cudaStream_t>(stream));
+                      o_sb, o_sh, nullptr, nullptr, static_cast<cudaStream_t>(stream), false);
 }
 
 extern "C" int bpt_merge_states(const float* o_part, const float* lse, int batch, int q_heads,
@@ -628,5 +691,5 @@ extern "C" int bpt_merge_states(const float* o_part, const float* lse, int batch
   if (batch == 0) return BPT_OK;
   if (!o_part || !lse || !o_out || !lse_out) return BPT_ERR_INVALID_ARGUMENT;
   return launch_merge(o_part, lse, batch, q_heads, splits, head_dim, nullptr, 0, 0, o_out,
-                      lse_out, static_cast<cudaStream_t>(stream));
+                      lse_out, static_cast<cudaStream_t>(stream), false);
 }

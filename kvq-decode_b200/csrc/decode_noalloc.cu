@@ -88,5 +88,5 @@ extern "C" int bpt_decode_fp16_noalloc(const void* q, int64_t q_sb, int64_t q_sh
                       nullptr, st);
   if (rc || S == 1) return rc;
   return launch_merge(o_part, lse, batch, q_heads, S, head_dim, static_cast<__half*>(out), o_sb,
-                      o_sh, nullptr, nullptr, st);
+                      o_sh, nullptr, nullptr, st, true);
 }

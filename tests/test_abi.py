@@ -41,15 +41,17 @@ def test_status_strings():
 
 def test_planner_fills_b200():
     from bpt.decode import choose_num_splits, effective_splits
-    # B=1, 64k tokens, bs=16: enough CTAs for 148 SMs
-    s = choose_num_splits(1, 8, 16, 4096, 148)
-    assert 8 * s >= 2 * 148
-    # large batch: no split needed
-    assert choose_num_splits(64, 8, 16, 4096, 148) <= 2
-    # short context caps the split count (>= 4 chunks of 64 tokens per split)
-    assert choose_num_splits(1, 8, 16, 16, 148) == 1
+    # B=1, 64k tokens, bs=16: one full wave of 4 CTAs/SM x 148 SMs (8 kv heads x 74 splits)
+    assert choose_num_splits(1, 8, 16, 4096, 148) == 74
+    # B=8: still one wave (64 x 9 = 576 <= 592)
+    assert choose_num_splits(8, 8, 16, 1024, 148) == 9
+    # B=64: fewer than 4 splits fit one wave -> ~8 waves of shorter CTAs
+    assert choose_num_splits(64, 8, 16, 4096, 148) == 10
+    # short context caps the split count (>= 2 chunks of 32 tokens per split)
+    assert choose_num_splits(1, 8, 16, 16, 148) == 4
+    assert choose_num_splits(1, 8, 16, 2, 148) == 1
     # explicit requests are clamped to the chunk count
-    assert effective_splits(2, 8, 16, 4, 7, 148) == 1
+    assert effective_splits(2, 8, 16, 4, 7, 148) == 2
     assert effective_splits(2, 8, 16, 512, 7, 148) == 7
     assert effective_splits(2, 8, 16, 512, 1, 148) == 1
 
