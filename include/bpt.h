@@ -105,6 +105,68 @@ int bpt_merge_partials(const float* o_part, const float* lse, int batch, int q_h
 int bpt_merge_states(const float* o_part, const float* lse, int batch, int q_heads,
                      int head_dim, int splits, float* o_out, float* lse_out, void* stream);
 
+/* ---------------------------------------------------------------- KIVI-quantized caches
+ *
+ * No counterpart in the reference (its README lists quantized KV as "not started"); the
+ * format follows the BASELINE KIVI description. Keys are quantized per (page, kv head,
+ * channel) over the page's tokens, values per (token, kv head) over the channels; INT8/INT4
+ * are asymmetric (unsigned codes, fp16 scale + zero-point, x ~= code * scale + zero), FP8-E4M3
+ * is symmetric (x ~= e4m3(code) * scale). Codes are computed from the fp16-rounded scale/zero
+ * with fp32 round-half-even arithmetic, bit-exact with the numpy specification in
+ * oracle/kivi.py. Storage, block_size = bs, H kv heads, D head dim:
+ *   INT8 / FP8  k_codes, v_codes [num_blocks, bs, H, D]   uint8
+ *   INT4        k_codes [num_blocks, bs, H, D/2]  (low nibble = even channel)
+ *               v_codes [num_blocks, bs/2, H, D]  (low nibble = even token)
+ *   k_scale, k_zero [num_blocks, H, D] fp16;  v_scale, v_zero [num_blocks, bs, H] fp16
+ *   (FP8: k_zero / v_zero unused, may be NULL).
+ * Strides are in elements of each array (bytes for the uint8 code arrays). */
+enum bpt_kv_format { BPT_KV_INT8 = 1, BPT_KV_FP8_E4M3 = 2, BPT_KV_INT4 = 3 };
+
+typedef struct bpt_kivi_cache {
+  int format;          /* enum bpt_kv_format */
+  int block_size;      /* tokens per page (power of two, 16..256; even for INT4) */
+  int kv_heads;
+  int head_dim;
+  int64_t num_blocks;
+  void* k_codes;  int64_t k_codes_stride[3];  /* block, token, head (inner stride 1) */
+  void* v_codes;  int64_t v_codes_stride[3];  /* block, token (INT4: token pair), head */
+  void* k_scale;  void* k_zero;  int64_t k_param_stride[2];  /* block, head */
+  void* v_scale;  void* v_zero;  int64_t v_param_stride[2];  /* block, token */
+} bpt_kivi_cache;
+
+/* Quantize and write new tokens into a KIVI cache (the cache-append step; no reference
+ * counterpart). Sequence b receives tokens [start_pos[b], start_pos[b] + new_lens[b]) from
+ * k_new / v_new [batch, max_new, H, D] fp16 (token t of the append at index t). start_pos[b]
+ * must be a multiple of block_size: key statistics are per page, so a page is always
+ * written whole from fp16 rows; slots past the appended tokens in the last page get code 0 and
+ * value scale/zero 0. new_lens / start_pos / block_table are device arrays. */
+int bpt_kivi_append(const bpt_kivi_cache* cache,
+                    const void* k_new, int64_t kn_sb, int64_t kn_st, int64_t kn_sh,
+                    const void* v_new, int64_t vn_sb, int64_t vn_st, int64_t vn_sh,
+                    const int32_t* new_lens, const int32_t* start_pos,
+                    const int32_t* block_table, int64_t bt_sb, int max_blocks,
+                    int batch, int max_new, void* stream);
+
+/* Fused-dequant decode over a KIVI cache: same contract as bpt_decode_fp16 (split
+ * semantics, workspace, status codes). The result equals fp32 attention over the dequantized
+ * cache (x_hat in fp32, never rounded to fp16): key scales are folded into q (q * scale as an
+ * fp16 hi + lo pair), value scales into the softmax weights, zero-points into fp32 bias terms.
+ * Built for head_dim 128 and group <= 8. No reference counterpart. */
+int bpt_decode_kivi(const bpt_kivi_cache* cache,
+                    const void* q, int64_t q_sb, int64_t q_sh,
+                    const int32_t* block_table, int64_t bt_sb, const int32_t* seq_lens,
+                    void* out, int64_t o_sb, int64_t o_sh,
+                    int batch, int q_heads, int max_blocks,
+                    float scale, int num_splits, int sm_count,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* Stage 1 alone over a KIVI cache, as bpt_decode_fp16_partial. */
+int bpt_decode_kivi_partial(const bpt_kivi_cache* cache,
+                            const void* q, int64_t q_sb, int64_t q_sh,
+                            const int32_t* block_table, int64_t bt_sb, const int32_t* seq_lens,
+                            int batch, int q_heads, int max_blocks, float scale, int splits,
+                            float* o_part, float* lse, unsigned* status, void* stream);
+
 /* Size of the fixed scratch array behind bpt_decode_fp16_noalloc, per GPU. */
 #define BPT_NOALLOC_SCRATCH_BYTES (8u * 1024u * 1024u)
 

@@ -34,6 +34,8 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 
 }  // namespace
 
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder_fn() { return tensor_map_encoder(); }
+
 int device_sm_count() {
   int dev = 0, sms = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 148;

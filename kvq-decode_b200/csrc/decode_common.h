@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -65,5 +66,9 @@ int run_split_fp16(const void* q, int64_t q_sb, int64_t q_sh, const void* k_cach
                    unsigned* status, cudaStream_t st);
 
 int device_sm_count();
+
+// cuTensorMapEncodeTiled resolved through the runtime's driver entry-point query (no link
+// dependency on libcuda); null if unavailable.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder_fn();
 
 }  // namespace bpt
