@@ -50,6 +50,12 @@ WORKLOADS = {
     "fp16_b1_ctx64k": dict(fmt="fp16", batch=1, ctx=65536, block_size=16, ragged=False),
     "fp16_b1_ctx128k": dict(fmt="fp16", batch=1, ctx=131072, block_size=16, ragged=False),
 }
+# BASELINE configs[3] (INT8 / FP8-E4M3 KIVI, bs=64) and configs[4] (INT4 KIVI, bs=64)
+for _fmt in ("int8", "fp8", "int4"):
+    for _b in (1, 8, 32, 64):
+        for _ctx, _tag in ((8192, "8k"), (32768, "32k"), (131072, "128k")):
+            WORKLOADS[f"{_fmt}_b{_b}_ctx{_tag}"] = dict(fmt=_fmt, batch=_b, ctx=_ctx,
+                                                        block_size=64, ragged=False)
 DEFAULT_WORKLOAD = "fp16_b64_ctx64k"
 # published reference number for the same metric (A100-80GB, best split, B=32 ctx=16k,
 # docs/NOTES.md:99 of the reference): 1638 GB/s
@@ -80,13 +86,22 @@ def workload_lens(wl, rank, seed):
     return [wl["ctx"]] * wl["batch"]
 
 
+def config_index(wl):
+    if wl["fmt"] == "fp16":
+        return 1 if wl["batch"] > 1 else 2
+    return 4 if wl["fmt"] == "int4" else 3
+
+
 def config_dict(name, wl, n_gpus):
     return {
-        "workload": f"{name}: BASELINE configs[{1 if wl['batch'] > 1 else 2}] "
+        "workload": f"{name}: BASELINE configs[{config_index(wl)}] "
                     f"{wl['fmt']} paged KV, Llama-3-8B layer (Hq={HQ}, Hkv={HKV}, D={D}), "
                     f"B={wl['batch']} per GPU, ctx={wl['ctx']}"
                     + (" seq_len~U[0.75ctx,ctx]" if wl["ragged"] else "")
-                    + f", block_size={wl['block_size']}, random-permutation block table",
+                    + f", block_size={wl['block_size']}, random-permutation block table"
+                    + ("" if wl["fmt"] == "fp16" else
+                       ", KIVI (keys per page/head/channel, values per token/head; K ~ N(0,1)"
+                       " with 4 seeded x10 outlier channels per kv head), quantized on the GPU"),
         "kv_dtype": wl["fmt"], "batch_per_gpu": wl["batch"], "ctx": wl["ctx"],
         "block_size": wl["block_size"], "q_heads": HQ, "kv_heads": HKV, "head_dim": D,
         "parallelism": f"batch-sharded x{n_gpus} (independent sequences per rank)",
@@ -175,32 +190,59 @@ class ClockSampler:
 
 # ----------------------------------------------------------------------------- CPU oracle
 
-def cpu_oracle_sample(lens, block_size, seed, budget_s, k_pages_fn=None):
-    """Time the numpy oracle (reference algorithm, src/bpt/reference.py:20-49) on a bounded
-    sample: whole sequences of the workload's length distribution, until ~budget_s seconds.
-    Returns (GB/s, seconds, bytes, description)."""
+def oracle_sample_inputs(n, block_size, fmt, seed):
+    """One sequence of n tokens for the CPU oracle: (q, k_cache, v_cache, bt, sl, nbytes_fn).
+    Quantized formats return the *codes* cache; the timed oracle step dequantizes it (the
+    reference's algorithm applied to the KIVI cache: dequantize, then fp32 attention)."""
     import numpy as np
-    from bpt.roofline import decode_call_bytes
-    from oracle import attention as oa
+    from oracle import kivi
     g = np.random.Generator(np.random.PCG64(seed))
-    n = int(lens[0])
     pages = (n + block_size - 1) // block_size
-    kc = g.standard_normal((pages, block_size, HKV, D), dtype=np.float32).astype(np.float16)
-    vc = g.standard_normal((pages, block_size, HKV, D), dtype=np.float32).astype(np.float16)
     q = g.standard_normal((1, HQ, D), dtype=np.float32).astype(np.float16)
     bt = g.permutation(pages).astype(np.int32)[None]
     sl = np.asarray([n], np.int32)
-    oa.paged_decode_attention_ref(q, kc, vc, bt, sl)  # warm-up
+    if fmt == "fp16":
+        kc = g.standard_normal((pages, block_size, HKV, D), dtype=np.float32).astype(np.float16)
+        vc = g.standard_normal((pages, block_size, HKV, D), dtype=np.float32).astype(np.float16)
+        return q, (kc, vc), bt, sl
+    cache = kivi.empty_cache(pages, block_size, HKV, D, fmt)
+    k = g.standard_normal((1, pages * block_size, HKV, D), dtype=np.float32)
+    k[..., :4] *= 10.0
+    v = g.standard_normal((1, pages * block_size, HKV, D), dtype=np.float32)
+    kivi.quantize_append(cache, k.astype(np.float16), v.astype(np.float16), [n], [0],
+                         bt, block_size, fmt)
+    return q, cache, bt, sl
+
+
+def oracle_step(q, kv, bt, sl, fmt):
+    from oracle import attention as oa
+    from oracle import kivi
+    import numpy as np
+    if fmt == "fp16":
+        return oa.paged_decode_attention_ref(q, kv[0], kv[1], bt, sl)
+    kd, vd = kivi.dequantize_cache(kv, fmt)
+    return oa.paged_decode_attention_ref(q, kd, vd, bt, sl, out_dtype=np.float16)
+
+
+def cpu_oracle_sample(lens, block_size, fmt, seed, budget_s):
+    """Time the CPU oracle (reference algorithm, src/bpt/reference.py:20-49; for KIVI caches
+    preceded by the numpy dequantization) on whole sequences of the workload's length (capped
+    at 32k tokens) until ~budget_s seconds. Returns (GB/s, seconds, bytes, description)."""
+    from bpt.roofline import decode_call_bytes
+    n = min(int(lens[0]), 32768)
+    q, kv, bt, sl = oracle_sample_inputs(n, block_size, fmt, seed)
+    oracle_step(q, kv, bt, sl, fmt)  # warm-up
     done, t0 = 0, time.perf_counter()
     while True:
-        oa.paged_decode_attention_ref(q, kc, vc, bt, sl)
+        oracle_step(q, kv, bt, sl, fmt)
         done += 1
         if time.perf_counter() - t0 > budget_s:
             break
     dt = time.perf_counter() - t0
-    nbytes = decode_call_bytes([n] * done, block_size, HQ, HKV, D, "fp16")
-    desc = (f"{done} x one sequence of {n} tokens (the workload's first length), numpy oracle "
-            f"(numpy BLAS threads = host cores)")
+    nbytes = decode_call_bytes([n] * done, block_size, HQ, HKV, D, fmt)
+    desc = (f"{done} x one sequence of {n} tokens ({fmt}), numpy oracle"
+            + ("" if fmt == "fp16" else " incl. numpy dequantization")
+            + " (numpy BLAS threads = host cores)")
     return nbytes / dt / 1e9, dt, nbytes, desc
 
 
@@ -211,29 +253,19 @@ def run_reference(args):
         return 0
     wl = WORKLOADS[args.workload]
     lens = workload_lens(wl, 0, args.seed)
-    import numpy as np
     from bpt.roofline import decode_call_bytes
-    from oracle import attention as oa
-    bs = wl["block_size"]
-    g = np.random.Generator(np.random.PCG64(args.seed))
-    # a pool of 2 sequences' pages; each step processes one whole sequence (rotating)
-    sample = [int(x) for x in lens[:2]]
-    pools = []
-    for n in sample:
-        pages = (n + bs - 1) // bs
-        kc = g.standard_normal((pages, bs, HKV, D), dtype=np.float32).astype(np.float16)
-        vc = g.standard_normal((pages, bs, HKV, D), dtype=np.float32).astype(np.float16)
-        q = g.standard_normal((1, HQ, D), dtype=np.float32).astype(np.float16)
-        bt = g.permutation(pages).astype(np.int32)[None]
-        pools.append((q, kc, vc, bt, np.asarray([n], np.int32)))
+    bs, fmt = wl["block_size"], wl["fmt"]
+    # a pool of 2 sequences; each step processes one whole sequence (rotating), capped at 32k
+    sample = [min(int(x), 32768) for x in (lens[:2] if len(lens) > 1 else lens * 2)]
+    pools = [oracle_sample_inputs(n, bs, fmt, args.seed + i) for i, n in enumerate(sample)]
     for i in range(args.warmup):
-        oa.paged_decode_attention_ref(*pools[i % len(pools)])
+        oracle_step(*pools[i % len(pools)], fmt)
     t0 = time.perf_counter()
     nbytes = 0
     for i in range(args.steps):
         p = pools[i % len(pools)]
-        oa.paged_decode_attention_ref(*p)
-        nbytes += decode_call_bytes([int(p[4][0])], bs, HQ, HKV, D, "fp16")
+        oracle_step(*p, fmt)
+        nbytes += decode_call_bytes([int(p[3][0])], bs, HQ, HKV, D, fmt)
     dt = time.perf_counter() - t0
     tbps = nbytes / dt / 1e12
     cores = os.cpu_count()
@@ -245,7 +277,7 @@ def run_reference(args):
         "config": config_dict(args.workload, wl, args.gpus),
         "cpu_baseline": {"value": tbps, "unit": "TB/s", "cores": cores, "kind": "port",
                          "sample": f"each step = one whole sequence of the workload "
-                                   f"({sample} tokens, rotating), numpy oracle"},
+                                   f"({sample} tokens, rotating; capped at 32k), numpy oracle"},
         "e2e": {"value": tbps, "unit": "TB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -278,10 +310,18 @@ def run_bpt(args):
                                 device_id=dev)
 
     wl = WORKLOADS[args.workload]
-    bs = wl["block_size"]
+    bs, fmt = wl["block_size"], wl["fmt"]
     lens = workload_lens(wl, rank, args.seed)
-    w = random_paged_workload(lens, HQ, HKV, D, bs, dev, seed=args.seed + rank, spare_blocks=64)
-    q, kc, vc, bt, sl = w["q"], w["k_cache"], w["v_cache"], w["block_table"], w["seq_lens"]
+    if fmt == "fp16":
+        w = random_paged_workload(lens, HQ, HKV, D, bs, dev, seed=args.seed + rank,
+                                  spare_blocks=64)
+        kc, vc = w["k_cache"], w["v_cache"]
+    else:
+        from bpt.quant import random_kivi_workload
+        w = random_kivi_workload(lens, HQ, HKV, D, bs, fmt, dev, seed=args.seed + rank,
+                                 spare_blocks=64)
+        kvcache = w["cache"]
+    q, bt, sl = w["q"], w["block_table"], w["seq_lens"]
     B = len(lens)
     max_blocks = bt.shape[1]
     sms = dec._sm_count(local)
@@ -296,7 +336,11 @@ def run_bpt(args):
 
     def call():
         # one product call: split-KV kernel (+ its programmatically dependent merge)
-        dec.paged_decode_attention(q, kc, vc, bt, sl, out=out, workspace=ws)
+        if fmt == "fp16":
+            dec.paged_decode_attention(q, kc, vc, bt, sl, out=out, workspace=ws)
+        else:
+            from bpt.quant import paged_decode_attention_kivi
+            paged_decode_attention_kivi(q, kvcache, bt, sl, out=out, workspace=ws)
 
     # The device-timed leg replays the call as a CUDA graph (what a serving engine does with a
     # decode step), so host-side Python cost does not leak into small workloads' timing.
@@ -370,7 +414,7 @@ def run_bpt(args):
             q.copy_(q_h, non_blocking=True)
             bt.copy_(bt_h, non_blocking=True)
             sl.copy_(sl_h, non_blocking=True)
-            dec.paged_decode_attention(q, kc, vc, bt, sl, out=out, workspace=ws)
+            call()
             out_h.copy_(out, non_blocking=True)
 
         for _ in range(max(args.warmup, 1)):
@@ -395,7 +439,7 @@ def run_bpt(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        gbps, secs, nbytes, desc = cpu_oracle_sample(lens, bs, args.seed, args.cpu_seconds)
+        gbps, secs, nbytes, desc = cpu_oracle_sample(lens, bs, fmt, args.seed, args.cpu_seconds)
         cpu = {"value": gbps / 1e3, "unit": "TB/s", "cores": os.cpu_count(), "kind": "port",
                "sample": desc, "seconds": round(secs, 2)}
 
@@ -417,7 +461,8 @@ def run_bpt(args):
         "scaling": "weak", "vs_baseline": value_tbps / REFERENCE_PUBLISHED_TBPS,
         "vs_baseline_ref": "reference's best published Triton FP16 figure, 1.638 TB/s "
                            "(A100-80GB, B=32 ctx=16k, docs/NOTES.md:99)",
-        "dtype": "f16", "data": "synthetic (seeded N(0,1) fp16 q/K/V, random block tables)",
+        "dtype": "f16" if fmt == "fp16" else f"{fmt} KV codes, f16 q/out, f32 math",
+        "data": "synthetic (seeded N(0,1) fp16 q/K/V, random block tables)",
         "config": config_dict(args.workload, wl, world),
         "pct_of_b200_spec_peak": 100.0 * value_tbps * 1e3 / (B200_SPEC_GBS * world),
         "us_per_decode_step": {"one_layer": ms_per_step * 1e3,
@@ -425,8 +470,9 @@ def run_bpt(args):
         "splits": S,
         "timing": "eager calls" if args.eager else "CUDA-graph replay of one product call per step",
         "roofline": {"bound": "hbm",
-                     "kernel": "split_kv_fp16_mma_kernel (+ PDL-chained merge_splits_kernel, "
-                               "<1% of the call; timed together per call)",
+                     "kernel": ("split_kv_fp16_mma_kernel" if fmt == "fp16" else
+                                f"kivi_decode_kernel<{fmt}>")
+                               + " (+ PDL-chained merge_splits_kernel; timed together per call)",
                      "achieved": achieved_gbs, "peak": peak, "unit": "GB/s",
                      "frac": achieved_gbs / peak, "peak_source": peak_src,
                      "traffic": traffic, "traffic_note": traffic_note,

@@ -270,5 +270,53 @@ def paged_decode_attention_kivi_partial(q: torch.Tensor, cache: KiviCache,
     return o_part, lse
 
 
+def random_kivi_workload(lens, q_heads: int, kv_heads: int, head_dim: int, block_size: int,
+                         fmt: str, device, seed: int = 0, outlier_channels: int = 4,
+                         outlier_scale: float = 10.0, spare_blocks: int = 0,
+                         seqs_per_batch: int = 4):
+    """Synthetic quantized decode inputs generated and quantized on ``device``.
+
+    K ~ N(0, 1) with ``outlier_channels`` seeded channels per kv head scaled by
+    ``outlier_scale``, V ~ N(0, 1), q ~ N(0, 1) (the BASELINE KIVI workload), quantized by the
+    cache-append kernel a few sequences at a time. Returns dict(q, cache, block_table,
+    seq_lens, num_blocks).
+    """
+    B = len(lens)
+    pages = [(int(n) + block_size - 1) // block_size for n in lens]
+    max_blocks = max(max(pages), 1)
+    num_blocks = sum(pages) + spare_blocks
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    perm = torch.randperm(num_blocks, generator=g)
+    bt = torch.zeros(B, max_blocks, dtype=torch.int32)
+    off = 0
+    for b, p in enumerate(pages):
+        bt[b, :p] = perm[off:off + p].to(torch.int32)
+        off += p
+    bt = bt.to(device)
+    mult = torch.ones(kv_heads, head_dim)
+    for h in range(kv_heads):
+        ch = torch.randperm(head_dim, generator=g)[:outlier_channels]
+        mult[h, ch] = outlier_scale
+    mult = mult.to(device)
+    cache = empty_kivi_cache(num_blocks, block_size, kv_heads, head_dim, fmt, device)
+    dg = torch.Generator(device=device).manual_seed(seed + 1)
+    q = torch.randn(B, q_heads, head_dim, generator=dg, device=device).to(torch.float16)
+    for b0 in range(0, B, seqs_per_batch):
+        sub = list(lens[b0:b0 + seqs_per_batch])
+        S = max(max(sub), 1)
+        k = torch.randn(len(sub), S, kv_heads, head_dim, generator=dg, device=device)
+        k = (k * mult).to(torch.float16)
+        v = torch.randn(len(sub), S, kv_heads, head_dim, generator=dg, device=device,
+                        dtype=torch.float16)
+        nl = torch.tensor(sub, dtype=torch.int32, device=device)
+        quantize_append(cache, k, v, nl, torch.zeros_like(nl),
+                        bt[b0:b0 + len(sub)].contiguous())
+        del k, v
+    return dict(q=q, cache=cache, block_table=bt,
+                seq_lens=torch.tensor(list(lens), dtype=torch.int32, device=device),
+                num_blocks=num_blocks)
+
+
 __all__ = ["KiviCache", "KiviCacheC", "empty_kivi_cache", "quantize_append", "FORMATS",
-           "paged_decode_attention_kivi", "paged_decode_attention_kivi_partial"]
+           "paged_decode_attention_kivi", "paged_decode_attention_kivi_partial",
+           "random_kivi_workload"]

@@ -575,8 +575,8 @@ kivi_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
         const uint32_t a1 = hsub_const<1024 + kC0Int4>((r8 & 0x000F000Fu) | kMagic);
         const uint32_t a2 = hsub_const<1024 + 16 * kC0Int4>((r & 0x00F000F0u) | kMagic);
         const uint32_t a3 = hsub_const<1024 + 16 * kC0Int4>((r8 & 0x00F000F0u) | kMagic);
-        mma_16816(acc[0][m], a0, a1, a2, a3, pb0, pb1);
-        if constexpr (G8) mma_16816(acc[C::NACC - 1][m], a0, a1, a2, a3, lo0, lo1);
+        mma::mma_16816_acc(acc[0][m], a0, a1, a2, a3, pb0, pb1);
+        if constexpr (G8) mma::mma_16816_acc(acc[C::NACC - 1][m], a0, a1, a2, a3, lo0, lo1);
       }
     } else {
       const int r0 = warp * 16 + tk, r1 = r0 + 1, r2 = r0 + 8, r3 = r0 + 9;
@@ -601,8 +601,8 @@ kivi_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
           a2 = hsub_const<1024 + kC0Int8>(__byte_perm(Y, kMagicBytes, 0x4140));
           a3 = hsub_const<1024 + kC0Int8>(__byte_perm(Y, kMagicBytes, 0x4342));
         }
-        mma_16816(acc[0][m], a0, a1, a2, a3, pb0, pb1);
-        if constexpr (G8) mma_16816(acc[C::NACC - 1][m], a0, a1, a2, a3, lo0, lo1);
+        mma::mma_16816_acc(acc[0][m], a0, a1, a2, a3, pb0, pb1);
+        if constexpr (G8) mma::mma_16816_acc(acc[C::NACC - 1][m], a0, a1, a2, a3, lo0, lo1);
       }
     }
     if (FP8 && lim < 16) mma::fence_proxy_async_smem();

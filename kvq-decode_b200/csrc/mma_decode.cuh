@@ -73,6 +73,29 @@ __device__ __forceinline__ void mma_16816(float (&c)[4], uint32_t a0, uint32_t a
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// d = A.B with a zero accumulator (a fresh partial product).
+__device__ __forceinline__ void mma_16816_zc(float (&d)[4], uint32_t a0, uint32_t a1,
+                                             uint32_t a2, uint32_t a3, uint32_t b0,
+                                             uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%10,%10,%10,%10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
+}
+
+// acc += A.B, with the product formed by the tensor core from a zero accumulator and added
+// in fp32 round-to-nearest: a long-running accumulator never passes through the tensor
+// core's own accumulation, whose per-step rounding would otherwise build up over thousands
+// of tokens on a large running sum.
+__device__ __forceinline__ void mma_16816_acc(float (&acc)[4], uint32_t a0, uint32_t a1,
+                                              uint32_t a2, uint32_t a3, uint32_t b0,
+                                              uint32_t b1) {
+  float t[4];
+  mma_16816_zc(t, a0, a1, a2, a3, b0, b1);
+  acc[0] += t[0]; acc[1] += t[1]; acc[2] += t[2]; acc[3] += t[3];
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
@@ -331,8 +354,8 @@ split_kv_fp16_mma_kernel(const __grid_constant__ CUtensorMap tmK,
       const uint32_t addr = vbase + uint32_t(db >> 2) * C::BLOCK_BYTES + ld_row + (chunk << 4);
       uint32_t a0, a1, a2, a3;
       ldsm_x4_trans(addr, a0, a1, a2, a3);
-      mma_16816(acc[0][db], a0, a1, a2, a3, pb0, pb1);
-      if constexpr (G8) mma_16816(acc[C::NACC - 1][db], a0, a1, a2, a3, lo0, lo1);
+      mma_16816_acc(acc[0][db], a0, a1, a2, a3, pb0, pb1);
+      if constexpr (G8) mma_16816_acc(acc[C::NACC - 1][db], a0, a1, a2, a3, lo0, lo1);
     }
     if (lim < 16) fence_proxy_async_smem();
     __syncwarp();

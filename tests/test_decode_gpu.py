@@ -215,3 +215,17 @@ def test_partial_states_and_merges(splits):
         c["q"], c["k_cache"], c["v_cache"], c["block_table"], lens, np.zeros_like(lens), lens)
     assert np.abs(o.cpu().numpy() - o_ref).max() < 1e-4
     assert np.abs(l2.cpu().numpy() - lse_ref * np.log2(np.e)).max() < 1e-4
+
+
+def test_long_biased_values_single_split():
+    """128k tokens of V ~ N(5, 1) in ONE split: every warp accumulates 64k tokens of positive
+    contributions in a single tensor-core accumulator; the result must stay within tolerance."""
+    from bpt import paged_decode_attention
+    from bpt.cache import random_paged_workload
+    w = random_paged_workload([131072], 32, 8, 128, 16, "cuda", seed=21)
+    w["v_cache"].add_(5.0)
+    ref = torch_reference(w["q"], w["k_cache"], w["v_cache"], w["block_table"], w["seq_lens"])
+    for ns in (1, None):
+        out = paged_decode_attention(w["q"], w["k_cache"], w["v_cache"], w["block_table"],
+                                     w["seq_lens"], num_splits=ns)
+        assert_close(out.float().cpu().numpy(), ref.cpu().numpy(), what=f"biased V ns={ns}")
