@@ -71,6 +71,9 @@ def parse():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--seqshard", action="store_true",
+                    help="shard every sequence's tokens over the ranks (strong scaling; the "
+                         "partial softmax states are merged with one NCCL all-gather)")
     ap.add_argument("--eager", action="store_true",
                     help="time eager calls instead of CUDA-graph replays of the call")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -92,7 +95,7 @@ def config_index(wl):
     return 4 if wl["fmt"] == "int4" else 3
 
 
-def config_dict(name, wl, n_gpus):
+def config_dict(name, wl, n_gpus, seqshard=False):
     return {
         "workload": f"{name}: BASELINE configs[{config_index(wl)}] "
                     f"{wl['fmt']} paged KV, Llama-3-8B layer (Hq={HQ}, Hkv={HKV}, D={D}), "
@@ -104,7 +107,10 @@ def config_dict(name, wl, n_gpus):
                        " with 4 seeded x10 outlier channels per kv head), quantized on the GPU"),
         "kv_dtype": wl["fmt"], "batch_per_gpu": wl["batch"], "ctx": wl["ctx"],
         "block_size": wl["block_size"], "q_heads": HQ, "kv_heads": HKV, "head_dim": D,
-        "parallelism": f"batch-sharded x{n_gpus} (independent sequences per rank)",
+        "parallelism": (f"sequence-sharded x{n_gpus} (page-aligned token ranges per rank, "
+                        f"partial softmax states merged after one NCCL all-gather)"
+                        if seqshard else
+                        f"batch-sharded x{n_gpus} (independent sequences per rank)"),
         "l2": "no flush: per-step working set (GBs of KV) far exceeds the 126 MB L2",
     }
 
@@ -311,7 +317,14 @@ def run_bpt(args):
 
     wl = WORKLOADS[args.workload]
     bs, fmt = wl["block_size"], wl["fmt"]
-    lens = workload_lens(wl, rank, args.seed)
+    seqshard = args.seqshard and world > 1
+    if seqshard:
+        from bpt.dist import decode_sequence_sharded, token_shards
+        full_lens = workload_lens(wl, 0, args.seed)          # same sequences on every rank
+        lens = [hi - lo for lo, hi in (token_shards(n, bs, world)[rank] for n in full_lens)]
+    else:
+        lens = workload_lens(wl, rank, args.seed)
+        full_lens = lens
     if fmt == "fp16":
         w = random_paged_workload(lens, HQ, HKV, D, bs, dev, seed=args.seed + rank,
                                   spare_blocks=64)
@@ -322,21 +335,32 @@ def run_bpt(args):
                                  spare_blocks=64)
         kvcache = w["cache"]
     q, bt, sl = w["q"], w["block_table"], w["seq_lens"]
+    if seqshard:  # every rank decodes the same queries against its own token shard
+        q = torch.randn(q.shape, generator=torch.Generator(device=dev).manual_seed(args.seed),
+                        device=dev).to(torch.float16)
     B = len(lens)
     max_blocks = bt.shape[1]
     sms = dec._sm_count(local)
     S = dec.effective_splits(B, HKV, bs, max_blocks, None, sms)
+    # algorithmic bytes of this rank's share of the job (seqshard: its tokens of the sequences,
+    # plus q/out once on rank 0 so the job total counts them once)
     step_bytes = decode_call_bytes(lens, bs, HQ, HKV, D, wl["fmt"])
+    if seqshard and rank != 0:
+        step_bytes -= len(lens) * HQ * D * 2 * 2
     f = KIVI_FORMATS[wl["fmt"]]
     kernel_bytes = step_bytes
     out = torch.empty_like(q)
     ws = torch.empty(dec.workspace_bytes(B, HQ, D, S), dtype=torch.uint8, device=dev)
-    launches_per_step = 2 if S > 1 else 1
+    launches_per_step = (2 if S > 1 else 1) + (2 if seqshard else 0)  # + state merge kernels
     stream = torch.cuda.current_stream(dev)
 
     def call():
         # one product call: split-KV kernel (+ its programmatically dependent merge)
-        if fmt == "fp16":
+        if seqshard:
+            decode_sequence_sharded(q, kc if fmt == "fp16" else None,
+                                    vc if fmt == "fp16" else None, bt, sl, out=out,
+                                    kivi_cache=None if fmt == "fp16" else kvcache)
+        elif fmt == "fp16":
             dec.paged_decode_attention(q, kc, vc, bt, sl, out=out, workspace=ws)
         else:
             from bpt.quant import paged_decode_attention_kivi
@@ -345,7 +369,7 @@ def run_bpt(args):
     # The device-timed leg replays the call as a CUDA graph (what a serving engine does with a
     # decode step), so host-side Python cost does not leak into small workloads' timing.
     graph = None
-    if not args.eager:
+    if not args.eager and not seqshard:  # sequence sharding includes an NCCL collective: eager
         call()
         torch.cuda.synchronize()
         side = torch.cuda.Stream(dev)
@@ -458,17 +482,19 @@ def run_bpt(args):
         "metric": metric_name(wl),
         "value": value_tbps, "unit": "TB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": value_tbps / REFERENCE_PUBLISHED_TBPS,
+        "scaling": "strong" if seqshard else "weak",
+        "vs_baseline": value_tbps / REFERENCE_PUBLISHED_TBPS,
         "vs_baseline_ref": "reference's best published Triton FP16 figure, 1.638 TB/s "
                            "(A100-80GB, B=32 ctx=16k, docs/NOTES.md:99)",
         "dtype": "f16" if fmt == "fp16" else f"{fmt} KV codes, f16 q/out, f32 math",
         "data": "synthetic (seeded N(0,1) fp16 q/K/V, random block tables)",
-        "config": config_dict(args.workload, wl, world),
+        "config": config_dict(args.workload, wl, world, seqshard),
         "pct_of_b200_spec_peak": 100.0 * value_tbps * 1e3 / (B200_SPEC_GBS * world),
         "us_per_decode_step": {"one_layer": ms_per_step * 1e3,
                                "llama3_8b_32_layers": ms_per_step * 1e3 * 32},
         "splits": S,
-        "timing": "eager calls" if args.eager else "CUDA-graph replay of one product call per step",
+        "timing": ("eager calls" if (args.eager or seqshard)
+                   else "CUDA-graph replay of one product call per step"),
         "roofline": {"bound": "hbm",
                      "kernel": ("split_kv_fp16_mma_kernel" if fmt == "fp16" else
                                 f"kivi_decode_kernel<{fmt}>")

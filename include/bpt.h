@@ -105,6 +105,14 @@ int bpt_merge_partials(const float* o_part, const float* lse, int batch, int q_h
 int bpt_merge_states(const float* o_part, const float* lse, int batch, int q_heads,
                      int head_dim, int splits, float* o_out, float* lse_out, void* stream);
 
+/* Cross-GPU merge of sequence-shard states. `states` holds `ranks` consecutive blocks (the
+ * output of an all-gather), each laid out as o [B, Hq, D] fp32 followed by lse [B, Hq]
+ * (log2 units) — exactly what bpt_merge_states writes for one rank's shard. The merged
+ * fp16 result goes to out [B, Hq, D]. No reference counterpart (the reference is single-GPU);
+ * the merge formula is the reference's split merge (src/bpt/triton_fp16.py:152-162). */
+int bpt_merge_rank_states(const float* states, int ranks, int batch, int q_heads,
+                          int head_dim, void* out, int64_t o_sb, int64_t o_sh, void* stream);
+
 /* ---------------------------------------------------------------- KIVI-quantized caches
  *
  * No counterpart in the reference (its README lists quantized KV as "not started"); the

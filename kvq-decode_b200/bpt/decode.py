@@ -212,6 +212,18 @@ def merge_states(o_part: torch.Tensor, lse: torch.Tensor):
              "o_part [B, Hq, S, D] and lse [B, Hq, S] must be contiguous")
     o = torch.empty(B, Hq, D, dtype=torch.float32, device=o_part.device)
     l2 = torch.empty(B, Hq, dtype=torch.float32, device=o_part.device)
+    return merge_states_into(o_part, lse, o, l2)
+
+
+def merge_states_into(o_part: torch.Tensor, lse: torch.Tensor, o: torch.Tensor,
+                      l2: torch.Tensor):
+    """``merge_states`` writing into caller tensors (contiguous fp32 [B, Hq, D], [B, Hq])."""
+    B, Hq, S, D = o_part.shape
+    _require(o_part.is_contiguous() and lse.is_contiguous() and lse.shape == (B, Hq, S),
+             "o_part [B, Hq, S, D] and lse [B, Hq, S] must be contiguous")
+    _require(o.shape == (B, Hq, D) and o.is_contiguous() and o.dtype == torch.float32 and
+             l2.shape == (B, Hq) and l2.is_contiguous() and l2.dtype == torch.float32,
+             "o must be contiguous fp32 [B, Hq, D] and l2 fp32 [B, Hq]")
     rc = _lib.lib().bpt_merge_states(o_part.data_ptr(), lse.data_ptr(), B, Hq, D, S,
                                      o.data_ptr(), l2.data_ptr(), _stream_handle(o_part.device))
     _lib.check(rc, "bpt_merge_states")

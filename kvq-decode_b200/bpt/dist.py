@@ -1,0 +1,153 @@
+"""Multi-GPU decode over one node: batch sharding and sequence sharding (no reference
+counterpart; the reference is single-GPU).
+
+One process per GPU, ``torch.distributed`` with the NCCL backend over NVLink / NVSwitch.
+
+* Batch sharding (B >= number of GPUs): each rank owns a contiguous slice of the sequences
+  together with their KV pages and block-table rows, and decodes them locally. Sequences are
+  independent, so there is no collective on the data path; ``gather_outputs`` optionally
+  all-gathers the [B_local, Hq, D] outputs for a consumer that needs all of them.
+
+* Sequence sharding (batch 1, long context): rank r owns the page-aligned token range
+  ``token_shards(...)[r]`` of every sequence in its own KV pool. Each rank runs the split-KV
+  kernel over its tokens and merges its splits into one fp32 state per (sequence, q head) --
+  o [B, Hq, D] and its log2-sum-exp [B, Hq] -- packed into one flat buffer; one
+  ``all_gather_into_tensor`` exchanges the states (B * Hq * (D + 1) * 4 bytes per rank, 16.5 KB
+  at the Llama-3-8B shape and B=1) and every rank merges the gathered states with the
+  reference's split-merge formula (src/bpt/triton_fp16.py:152-162) into the fp16 output.
+  All ranks take the same collective steps in the same order; a rank that fails or never
+  joins surfaces as the process group's timeout error on the others.
+"""
+import ctypes
+from typing import List, Optional, Sequence, Tuple
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from ._lib import BptArgumentError
+from .decode import _require, _stream_handle, merge_states_into, paged_decode_attention, \
+    paged_decode_attention_partial
+
+
+def shard_range(n: int, world: int, rank: int) -> Tuple[int, int]:
+    """Contiguous balanced [lo, hi) slice of n items for `rank` of `world`."""
+    _require(world >= 1 and 0 <= rank < world, "bad world/rank")
+    return (n * rank) // world, (n * (rank + 1)) // world
+
+
+def token_shards(seq_len: int, block_size: int, world: int) -> List[Tuple[int, int]]:
+    """Page-aligned token ranges [lo, hi) covering a sequence, one per rank (balanced by
+    pages; a rank may get an empty range when there are fewer pages than ranks)."""
+    pages = (int(seq_len) + block_size - 1) // block_size
+    out = []
+    for r in range(world):
+        p0, p1 = shard_range(pages, world, r)
+        out.append((min(p0 * block_size, seq_len), min(p1 * block_size, seq_len)))
+    return out
+
+
+_MERGE_RANKS = None
+
+
+def _merge_ranks_fn():
+    global _MERGE_RANKS
+    if _MERGE_RANKS is None:
+        _MERGE_RANKS = _lib.register("bpt_merge_rank_states", ctypes.c_int, [
+            ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+            ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p])
+    return _MERGE_RANKS
+
+
+def state_buffer(batch: int, q_heads: int, head_dim: int, device) -> torch.Tensor:
+    """Flat fp32 buffer holding one rank's state: o [B, Hq, D] then lse [B, Hq]."""
+    return torch.empty(batch * q_heads * (head_dim + 1), dtype=torch.float32, device=device)
+
+
+def split_state(buf: torch.Tensor, batch: int, q_heads: int, head_dim: int):
+    n = batch * q_heads * head_dim
+    return buf[:n].view(batch, q_heads, head_dim), buf[n:].view(batch, q_heads)
+
+
+def merge_rank_states(gathered: torch.Tensor, ranks: int, batch: int, q_heads: int,
+                      head_dim: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Merge `ranks` gathered state blocks [ranks * B*Hq*(D+1)] into fp16 [B, Hq, D]."""
+    _require(gathered.is_cuda and gathered.dtype == torch.float32 and gathered.is_contiguous(),
+             "gathered states must be a contiguous fp32 CUDA tensor")
+    _require(gathered.numel() == ranks * batch * q_heads * (head_dim + 1),
+             "gathered states have the wrong size")
+    if out is None:
+        out = torch.empty(batch, q_heads, head_dim, dtype=torch.float16, device=gathered.device)
+    rc = _merge_ranks_fn()(gathered.data_ptr(), ranks, batch, q_heads, head_dim, out.data_ptr(),
+                           out.stride(0), out.stride(1), _stream_handle(gathered.device))
+    _lib.check(rc, "bpt_merge_rank_states")
+    return out
+
+
+def local_state(q: torch.Tensor, k_cache, v_cache, block_table: torch.Tensor,
+                seq_lens: torch.Tensor, scale: Optional[float] = None,
+                num_splits: Optional[int] = None, out_state: Optional[torch.Tensor] = None,
+                kivi_cache=None) -> torch.Tensor:
+    """This rank's merged fp32 state over its own tokens, packed for the all-gather.
+
+    FP16 caches pass k_cache / v_cache; KIVI caches pass kivi_cache (k_cache = v_cache = None).
+    """
+    B, Hq, D = q.shape
+    if kivi_cache is not None:
+        from .quant import paged_decode_attention_kivi_partial
+        o_part, lse = paged_decode_attention_kivi_partial(q, kivi_cache, block_table, seq_lens,
+                                                          scale, num_splits)
+    else:
+        o_part, lse = paged_decode_attention_partial(q, k_cache, v_cache, block_table,
+                                                     seq_lens, scale, num_splits)
+    if out_state is None:
+        out_state = state_buffer(B, Hq, D, q.device)
+    o, l2 = split_state(out_state, B, Hq, D)
+    merge_states_into(o_part, lse, o, l2)
+    return out_state
+
+
+def decode_sequence_sharded(q: torch.Tensor, k_cache, v_cache, block_table: torch.Tensor,
+                            seq_lens: torch.Tensor, scale: Optional[float] = None,
+                            num_splits: Optional[int] = None, *, group=None, kivi_cache=None,
+                            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Decode sequences whose tokens are spread over the ranks of `group`.
+
+    Every rank passes the same q [B, Hq, D] and ITS OWN pages: block_table / seq_lens describe
+    the rank's token range of each sequence (seq_lens[b] = tokens this rank holds, may be 0).
+    Returns the full fp16 [B, Hq, D] result on every rank.
+    """
+    world = dist.get_world_size(group)
+    B, Hq, D = q.shape
+    send = local_state(q, k_cache, v_cache, block_table, seq_lens, scale, num_splits,
+                       kivi_cache=kivi_cache)
+    recv = torch.empty(world * send.numel(), dtype=torch.float32, device=q.device)
+    dist.all_gather_into_tensor(recv, send, group=group)
+    return merge_rank_states(recv, world, B, Hq, D, out=out)
+
+
+def decode_batch_sharded(q_local: torch.Tensor, k_cache, v_cache, block_table: torch.Tensor,
+                         seq_lens: torch.Tensor, scale: Optional[float] = None,
+                         num_splits: Optional[int] = None, *, kivi_cache=None,
+                         out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Decode this rank's slice of the batch (its own sequences, pages and table rows).
+    No communication: batch sharding needs none."""
+    if kivi_cache is not None:
+        from .quant import paged_decode_attention_kivi
+        return paged_decode_attention_kivi(q_local, kivi_cache, block_table, seq_lens, scale,
+                                           num_splits, out=out)
+    return paged_decode_attention(q_local, k_cache, v_cache, block_table, seq_lens, scale,
+                                  num_splits, out=out)
+
+
+def gather_outputs(out_local: torch.Tensor, group=None) -> torch.Tensor:
+    """All-gather equal-sized [B_local, Hq, D] outputs of a batch-sharded decode."""
+    world = dist.get_world_size(group)
+    res = torch.empty((world * out_local.shape[0],) + tuple(out_local.shape[1:]),
+                      dtype=out_local.dtype, device=out_local.device)
+    dist.all_gather_into_tensor(res, out_local.contiguous(), group=group)
+    return res
+
+
+__all__ = ["shard_range", "token_shards", "state_buffer", "split_state", "merge_rank_states",
+           "local_state", "decode_sequence_sharded", "decode_batch_sharded", "gather_outputs"]

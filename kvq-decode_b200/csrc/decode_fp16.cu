@@ -398,23 +398,31 @@ split_kv_fp16_kernel(const __grid_constant__ CUtensorMap tmK,
 }
 
 // Stage 2: out = sum_s w_s o_s / sum_s w_s, w_s = 2^(lse_s - max lse) (lse in log2 units).
+// The partial states are addressed through strides (elements) so the same kernel merges the
+// split partials [B, Hq, S, D] of one call and rank states gathered as [S ranks, B, Hq, ...].
 // F16OUT: write the normalised fp16 output; otherwise write the merged fp32 state (o, lse),
 // which is what a cross-GPU merge of sequence shards consumes.
+struct MergeLayout {
+  int64_t o_ss, o_sb, o_sh;   // partial o: split, batch, head strides (d stride 1)
+  int64_t l_ss, l_sb, l_sh;   // partial lse strides
+};
+
 template <bool F16OUT>
 __global__ void __launch_bounds__(128)
 merge_splits_kernel(const float* __restrict__ o_part, const float* __restrict__ lse,
-                    int q_heads, int splits, int D, __half* __restrict__ out16, int64_t o_sb,
-                    int64_t o_sh, float* __restrict__ o32, float* __restrict__ lse32) {
+                    const MergeLayout lay, int q_heads, int splits, int D,
+                    __half* __restrict__ out16, int64_t o_sb, int64_t o_sh,
+                    float* __restrict__ o32, float* __restrict__ lse32) {
   extern __shared__ float w_s[];  // [splits]
   __shared__ float red[4];
   const int hq = blockIdx.x, b = blockIdx.y;
-  const int64_t row0 = (int64_t(b) * q_heads + hq) * splits;
-  const float* l = lse + row0;
+  const float* l = lse + int64_t(b) * lay.l_sb + int64_t(hq) * lay.l_sh;
+  const float* o = o_part + int64_t(b) * lay.o_sb + int64_t(hq) * lay.o_sh;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   pdl_wait();
 
   float m = kNegInf;
-  for (int s = tid; s < splits; s += blockDim.x) m = fmaxf(m, l[s]);
+  for (int s = tid; s < splits; s += blockDim.x) m = fmaxf(m, l[s * lay.l_ss]);
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(kFullMask, m, off));
   if (lane == 0) red[warp] = m;
@@ -423,7 +431,7 @@ merge_splits_kernel(const float* __restrict__ o_part, const float* __restrict__ 
   __syncthreads();
   float wsum = 0.f;
   for (int s = tid; s < splits; s += blockDim.x) {
-    const float w = (M == kNegInf) ? 0.f : fast_exp2(l[s] - M);
+    const float w = (M == kNegInf) ? 0.f : fast_exp2(l[s * lay.l_ss] - M);
     w_s[s] = w;
     wsum += w;
   }
@@ -436,13 +444,13 @@ merge_splits_kernel(const float* __restrict__ o_part, const float* __restrict__ 
     float a = 0.f;
     for (int s = 0; s < splits; ++s) {
       const float w = w_s[s];
-      if (w != 0.f) a = fmaf(w, o_part[(row0 + s) * D + d], a);
+      if (w != 0.f) a = fmaf(w, o[s * lay.o_ss + d], a);
     }
-    const float o = W > 0.f ? a / W : 0.f;
+    const float r = W > 0.f ? a / W : 0.f;
     if constexpr (F16OUT) {
-      out16[int64_t(b) * o_sb + int64_t(hq) * o_sh + d] = __float2half_rn(o);
+      out16[int64_t(b) * o_sb + int64_t(hq) * o_sh + d] = __float2half_rn(r);
     } else {
-      o32[(int64_t(b) * q_heads + hq) * D + d] = o;
+      o32[(int64_t(b) * q_heads + hq) * D + d] = r;
     }
   }
   if constexpr (!F16OUT) {
@@ -517,9 +525,10 @@ int tc_chunk_tokens(int head_dim) {
 
 }  // namespace
 
-int launch_merge(const float* o_part, const float* lse, int batch, int q_heads, int splits,
-                 int D, __half* out16, int64_t o_sb, int64_t o_sh, float* o32, float* lse32,
-                 cudaStream_t st, bool pdl) {
+static int launch_merge_layout(const float* o_part, const float* lse, const MergeLayout& lay,
+                               int batch, int q_heads, int splits, int D, __half* out16,
+                               int64_t o_sb, int64_t o_sh, float* o32, float* lse32,
+                               cudaStream_t st, bool pdl) {
   if (batch <= 0) return BPT_OK;
   const size_t sm = size_t(splits) * sizeof(float);
   if (sm > 48 * 1024) return BPT_ERR_UNSUPPORTED_SHAPE;
@@ -535,14 +544,28 @@ int launch_merge(const float* o_part, const float* lse, int batch, int q_heads, 
   cfg.numAttrs = pdl ? 1 : 0;
   cudaError_t e;
   if (out16) {
-    e = cudaLaunchKernelEx(&cfg, merge_splits_kernel<true>, o_part, lse, q_heads, splits, D,
-                           out16, o_sb, o_sh, static_cast<float*>(nullptr),
+    e = cudaLaunchKernelEx(&cfg, merge_splits_kernel<true>, o_part, lse, lay, q_heads, splits,
+                           D, out16, o_sb, o_sh, static_cast<float*>(nullptr),
                            static_cast<float*>(nullptr));
   } else {
-    e = cudaLaunchKernelEx(&cfg, merge_splits_kernel<false>, o_part, lse, q_heads, splits, D,
-                           static_cast<__half*>(nullptr), int64_t(0), int64_t(0), o32, lse32);
+    e = cudaLaunchKernelEx(&cfg, merge_splits_kernel<false>, o_part, lse, lay, q_heads, splits,
+                           D, static_cast<__half*>(nullptr), int64_t(0), int64_t(0), o32, lse32);
   }
   return e == cudaSuccess ? BPT_OK : BPT_ERR_LAUNCH;
+}
+
+int launch_merge(const float* o_part, const float* lse, int batch, int q_heads, int splits,
+                 int D, __half* out16, int64_t o_sb, int64_t o_sh, float* o32, float* lse32,
+                 cudaStream_t st, bool pdl) {
+  MergeLayout lay;  // [B, Hq, S, D] partials of one call
+  lay.o_ss = D;
+  lay.o_sh = int64_t(splits) * D;
+  lay.o_sb = int64_t(q_heads) * splits * D;
+  lay.l_ss = 1;
+  lay.l_sh = splits;
+  lay.l_sb = int64_t(q_heads) * splits;
+  return launch_merge_layout(o_part, lse, lay, batch, q_heads, splits, D, out16, o_sb, o_sh, o32,
+                             lse32, st, pdl);
 }
 
 // Validate, encode the tensor maps and launch the split kernel. `final_out` selects the
@@ -692,4 +715,25 @@ extern "C" int bpt_merge_states(const float* o_part, const float* lse, int batch
   if (!o_part || !lse || !o_out || !lse_out) return BPT_ERR_INVALID_ARGUMENT;
   return launch_merge(o_part, lse, batch, q_heads, splits, head_dim, nullptr, 0, 0, o_out,
                       lse_out, static_cast<cudaStream_t>(stream), false);
+}
+
+extern "C" int bpt_merge_rank_states(const float* states, int ranks, int batch, int q_heads,
+                                     int head_dim, void* out, int64_t o_sb, int64_t o_sh,
+                                     void* stream) {
+  if (ranks < 1 || batch < 0 || q_heads <= 0 || head_dim <= 0) return BPT_ERR_INVALID_ARGUMENT;
+  if (batch == 0) return BPT_OK;
+  if (!states || !out) return BPT_ERR_INVALID_ARGUMENT;
+  // each rank's block: o [B, Hq, D] then lse [B, Hq]
+  const int64_t block = int64_t(batch) * q_heads * (head_dim + 1);
+  MergeLayout lay;
+  lay.o_ss = block;
+  lay.o_sb = int64_t(q_heads) * head_dim;
+  lay.o_sh = head_dim;
+  lay.l_ss = block;
+  lay.l_sb = q_heads;
+  lay.l_sh = 1;
+  const float* lse = states + int64_t(batch) * q_heads * head_dim;
+  return launch_merge_layout(states, lse, lay, batch, q_heads, ranks, head_dim,
+                             static_cast<__half*>(out), o_sb, o_sh, nullptr, nullptr,
+                             static_cast<cudaStream_t>(stream), false);
 }
