@@ -136,6 +136,24 @@ def ncu_traffic(workload):
         return None, None
 
 
+class quiet_stdout:
+    """Silence file descriptor 1 (C/C++ writes included, e.g. NCCL's version banner at
+    communicator creation) so rank 0 prints exactly one JSON line on stdout."""
+
+    def __enter__(self):
+        sys.stdout.flush()
+        self.saved = os.dup(1)
+        self.null = os.open(os.devnull, os.O_WRONLY)
+        os.dup2(self.null, 1)
+        return self
+
+    def __exit__(self, *a):
+        sys.stdout.flush()
+        os.dup2(self.saved, 1)
+        os.close(self.saved)
+        os.close(self.null)
+
+
 class ClockSampler:
     """NVML SM-clock and clock-event-reason sampling while the timed region runs."""
     REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
@@ -312,8 +330,10 @@ def run_bpt(args):
     dev = torch.device("cuda", local)
     if world > 1:
         import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=dev)
+        with quiet_stdout():
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=dev)
+            dist.barrier(device_ids=[local])  # creates the communicator
 
     wl = WORKLOADS[args.workload]
     bs, fmt = wl["block_size"], wl["fmt"]
