@@ -361,7 +361,11 @@ def run_bpt(args):
     B = len(lens)
     max_blocks = bt.shape[1]
     sms = dec._sm_count(local)
-    S = dec.effective_splits(B, HKV, bs, max_blocks, None, sms)
+    if wl["fmt"] == "fp16":
+        S = dec.effective_splits(B, HKV, bs, max_blocks, None, sms)
+    else:
+        from bpt.quant import effective_splits_kivi
+        S = effective_splits_kivi(kvcache, B, HQ, max_blocks, None, sms)
     # algorithmic bytes of this rank's share of the job (seqshard: its tokens of the sequences,
     # plus q/out once on rank 0 so the job total counts them once)
     step_bytes = decode_call_bytes(lens, bs, HQ, HKV, D, wl["fmt"])

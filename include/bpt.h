@@ -155,11 +155,19 @@ int bpt_kivi_append(const bpt_kivi_cache* cache,
                     const int32_t* block_table, int64_t bt_sb, int max_blocks,
                     int batch, int max_new, void* stream);
 
+/* Split count a KIVI decode call uses for a requested num_splits (<= 0 = heuristic), as
+ * bpt_effective_splits for the kernel that serves this format and group (its tokens per
+ * pipeline stage and CTAs per SM differ from the fp16 kernel's). No reference counterpart. */
+int bpt_effective_splits_kivi(int format, int batch, int kv_heads, int q_heads, int block_size,
+                              int max_blocks, int num_splits, int sm_count);
+
 /* Fused-dequant decode over a KIVI cache: same contract as bpt_decode_fp16 (split
- * semantics, workspace, status codes). The result equals fp32 attention over the dequantized
- * cache (x_hat in fp32, never rounded to fp16): key scales are folded into q (q * scale as an
- * fp16 hi + lo pair), value scales into the softmax weights, zero-points into fp32 bias terms.
- * Built for head_dim 128 and group <= 8. No reference counterpart. */
+ * semantics, workspace, status codes), with splits from bpt_effective_splits_kivi. The result
+ * equals fp32 attention over the dequantized cache (x_hat in fp32, never rounded to fp16):
+ * key scales are folded into q, value scales into the softmax weights, zero-points into fp32
+ * bias terms. INT8 / INT4 with group <= 4 run on integer tensor-core MMAs (q * scale and
+ * p * scale as exact-accumulated fixed point); FP8 and larger groups on fp16 MMAs (hi + lo
+ * fp16 pairs). Built for head_dim 128 and group <= 8. No reference counterpart. */
 int bpt_decode_kivi(const bpt_kivi_cache* cache,
                     const void* q, int64_t q_sb, int64_t q_sh,
                     const int32_t* block_table, int64_t bt_sb, const int32_t* seq_lens,

@@ -193,6 +193,20 @@ def _decode_fns():
     return _DECODE, _DECODE_PARTIAL
 
 
+_SPLITS = None
+
+
+def effective_splits_kivi(cache: "KiviCache", batch: int, q_heads: int, max_blocks: int,
+                          num_splits: Optional[int], sm_count: int) -> int:
+    """Split count a KIVI decode call uses (bpt_effective_splits_kivi): the kernel serving
+    the format / group has its own tokens per stage and CTAs per SM."""
+    global _SPLITS
+    if _SPLITS is None:
+        _SPLITS = _lib.register("bpt_effective_splits_kivi", c_i32, [c_i32] * 8)
+    return int(_SPLITS(FORMATS[cache.fmt], batch, cache.kv_heads, q_heads, cache.block_size,
+                       max_blocks, int(num_splits or 0), sm_count))
+
+
 def _validate_decode(q, cache: KiviCache, block_table, seq_lens):
     _require(q.dim() == 3 and q.dtype == torch.float16 and q.stride(2) == 1,
              "q must be float16 [B, Hq, D] with unit inner stride")
@@ -222,12 +236,12 @@ def paged_decode_attention_kivi(q: torch.Tensor, cache: KiviCache, block_table: 
     Same contract as ``bpt.paged_decode_attention`` (split semantics, no host sync, zeros for
     an empty sequence); matches fp32 attention on the dequantized cache.
     """
-    from .decode import effective_splits, workspace_bytes
+    from .decode import workspace_bytes
     B, Hq, D = _validate_decode(q, cache, block_table, seq_lens)
     dev = q.device
     sms = _sm_count(dev.index or 0)
     max_blocks = block_table.shape[1]
-    S = effective_splits(B, cache.kv_heads, cache.block_size, max_blocks, num_splits, sms)
+    S = effective_splits_kivi(cache, B, Hq, max_blocks, num_splits, sms)
     need = workspace_bytes(B, Hq, D, S)
     if workspace is None or workspace.numel() * workspace.element_size() < need:
         workspace = torch.empty(need, dtype=torch.uint8, device=dev)
@@ -253,11 +267,10 @@ def paged_decode_attention_kivi_partial(q: torch.Tensor, cache: KiviCache,
                                         scale: Optional[float] = None,
                                         num_splits: Optional[int] = None):
     """Stage 1 only over a KIVI cache: (o_part [B, Hq, S, D] fp32, lse [B, Hq, S] log2)."""
-    from .decode import effective_splits
     B, Hq, D = _validate_decode(q, cache, block_table, seq_lens)
     dev = q.device
-    S = effective_splits(B, cache.kv_heads, cache.block_size, block_table.shape[1], num_splits,
-                         _sm_count(dev.index or 0))
+    S = effective_splits_kivi(cache, B, Hq, block_table.shape[1], num_splits,
+                              _sm_count(dev.index or 0))
     o_part = torch.empty(B, Hq, S, D, dtype=torch.float32, device=dev)
     lse = torch.empty(B, Hq, S, dtype=torch.float32, device=dev)
     c = cache.to_c()
@@ -319,4 +332,5 @@ def random_kivi_workload(lens, q_heads: int, kv_heads: int, head_dim: int, block
 
 __all__ = ["KiviCache", "KiviCacheC", "empty_kivi_cache", "quantize_append", "FORMATS",
            "paged_decode_attention_kivi", "paged_decode_attention_kivi_partial",
+           "effective_splits_kivi",
            "random_kivi_workload"]

@@ -106,16 +106,18 @@ extern "C" const char* bpt_status_string(int status) {
 
 extern "C" int bpt_version(void) { return 100; }
 
-extern "C" int bpt_plan_splits(int batch, int kv_heads, int block_size, int max_blocks,
-                               int sm_count) {
-  // One CTA per (sequence, kv head, split); kResidentCtas of them fit on an SM at once.
+namespace bpt {
+
+int plan_splits(int batch, int kv_heads, int block_size, int max_blocks, int sm_count,
+                int resident_per_sm, int chunk_tokens) {
+  // One CTA per (sequence, kv head, split); resident_per_sm of them fit on an SM at once.
   // If at least 4 splits still fit in ONE wave, use exactly that many (every CTA starts
   // together, no tail); otherwise aim for ~8 waves of shorter CTAs so the ragged tail is
   // small. Never split below 2 chunks per split.
   if (sm_count <= 0) sm_count = device_sm_count();
-  const int64_t units = (int64_t(max_blocks) * block_size + kChunkTokens - 1) / kChunkTokens;
+  const int64_t units = (int64_t(max_blocks) * block_size + chunk_tokens - 1) / chunk_tokens;
   const int64_t work = int64_t(batch > 0 ? batch : 1) * (kv_heads > 0 ? kv_heads : 1);
-  const int64_t resident = int64_t(sm_count) * kResidentCtas;
+  const int64_t resident = int64_t(sm_count) * resident_per_sm;
   int64_t want = resident / work;
   if (want < kMinSingleWaveSplits) want = (kWaves * resident + work - 1) / work;
   int64_t cap = units / kMinChunksPerSplit;
@@ -125,14 +127,27 @@ extern "C" int bpt_plan_splits(int batch, int kv_heads, int block_size, int max_
   return int(want);
 }
 
-extern "C" int bpt_effective_splits(int batch, int kv_heads, int block_size, int max_blocks,
-                                    int num_splits, int sm_count) {
-  int s = num_splits > 0 ? num_splits
-                         : bpt_plan_splits(batch, kv_heads, block_size, max_blocks, sm_count);
-  const int64_t units = (int64_t(max_blocks) * block_size + kChunkTokens - 1) / kChunkTokens;
+int clamp_splits(int s, int block_size, int max_blocks, int chunk_tokens) {
+  const int64_t units = (int64_t(max_blocks) * block_size + chunk_tokens - 1) / chunk_tokens;
   if (s > units) s = int(units);
   if (s < 1) s = 1;
   return s;
+}
+
+}  // namespace bpt
+
+extern "C" int bpt_plan_splits(int batch, int kv_heads, int block_size, int max_blocks,
+                               int sm_count) {
+  return plan_splits(batch, kv_heads, block_size, max_blocks, sm_count, kResidentCtas,
+                     kChunkTokens);
+}
+
+extern "C" int bpt_effective_splits(int batch, int kv_heads, int block_size, int max_blocks,
+                                    int num_splits, int sm_count) {
+  const int s = num_splits > 0
+                    ? num_splits
+                    : bpt_plan_splits(batch, kv_heads, block_size, max_blocks, sm_count);
+  return clamp_splits(s, block_size, max_blocks, kChunkTokens);
 }
 
 extern "C" size_t bpt_decode_workspace_bytes(int batch, int q_heads, int head_dim, int splits) {

@@ -66,6 +66,11 @@ int run_split_fp16(const void* q, int64_t q_sb, int64_t q_sh, const void* k_cach
                    unsigned* status, cudaStream_t st);
 
 int device_sm_count();
+// Split planner for a kernel with `resident_per_sm` CTAs per SM and `chunk_tokens` tokens per
+// pipeline stage (splits are whole chunks); clamp_splits bounds a requested count.
+int plan_splits(int batch, int kv_heads, int block_size, int max_blocks, int sm_count,
+                int resident_per_sm, int chunk_tokens);
+int clamp_splits(int s, int block_size, int max_blocks, int chunk_tokens);
 
 // cuTensorMapEncodeTiled resolved through the runtime's driver entry-point query (no link
 // dependency on libcuda); null if unavailable.

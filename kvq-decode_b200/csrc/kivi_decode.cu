@@ -77,6 +77,7 @@ struct KiviParams {
   const uint8_t* v_scale;   // v_scale / v_zero base (element 0 is 4-byte aligned)
   const uint8_t* v_zero;
   int64_t vps0, vps1;       // element strides (block, token); head stride 1
+  int lbs, lbox;            // log2 of block_size and of the TMA box rows
 };
 
 // Integer codes enter the MMA centred (code - C0), so the fp32 accumulator sums
@@ -697,6 +698,91 @@ int launch(const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tks,
   return BPT_OK;
 }
 
+#include "kivi_int.cuh"
+
+#ifndef BPT_KIVI_INT8_STAGES
+#define BPT_KIVI_INT8_STAGES 3
+#endif
+#ifndef BPT_KIVI_INT4_STAGES
+#define BPT_KIVI_INT4_STAGES 3
+#endif
+#ifndef BPT_KIVI_INT_MINB
+#define BPT_KIVI_INT_MINB 3
+#endif
+
+#include "kivi_tc.cuh"
+
+#ifndef BPT_KIVI_TC_KSLOTS
+#define BPT_KIVI_TC_KSLOTS 2
+#endif
+#ifndef BPT_KIVI_TC_VSLOTS
+#define BPT_KIVI_TC_VSLOTS 3
+#endif
+#ifndef BPT_KIVI_TC_MINB
+#define BPT_KIVI_TC_MINB 2
+#endif
+
+template <int FMT>
+using TcCfg = TCfg<FMT, BPT_KIVI_TC_KSLOTS, BPT_KIVI_TC_VSLOTS>;
+
+template <int FMT>
+using IntCfg =
+    ICfg<FMT, FMT == BPT_KV_INT4 ? BPT_KIVI_INT4_STAGES : BPT_KIVI_INT8_STAGES>;
+
+constexpr int kSmemPerSm = 228 * 1024;   // shared memory of one B200 SM
+constexpr int kSmemPerCtaReserved = 1024;
+
+template <int FMT>
+int int_resident_ctas(int block_size) {
+  using C = IntCfg<FMT>;
+  const int box = block_size < C::CHUNK ? block_size : C::CHUNK;
+  const int per = int(C::smem_bytes(C::CHUNK / box)) + kSmemPerCtaReserved;
+  int r = kSmemPerSm / per;
+  if (r > BPT_KIVI_INT_MINB) r = BPT_KIVI_INT_MINB;
+  return r < 1 ? 1 : r;
+}
+
+template <int FMT>
+int tc_resident_ctas(int block_size) {
+  using C = TcCfg<FMT>;
+  const int box = block_size < C::CHUNK ? block_size : C::CHUNK;
+  const int per = int(C::smem_bytes(C::CHUNK / box)) + kSmemPerCtaReserved;
+  int r = kSmemPerSm / per;
+  if (r > BPT_KIVI_TC_MINB) r = BPT_KIVI_TC_MINB;
+  return r < 1 ? 1 : r;
+}
+
+template <int FMT>
+int launch_tc(const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tks,
+              const CUtensorMap& tkz, const CUtensorMap& tvs, const CUtensorMap& tvz,
+              const KiviParams& kp, cudaStream_t st) {
+  using C = TcCfg<FMT>;
+  auto kern = kivi_tc_decode_kernel<FMT, BPT_KIVI_TC_KSLOTS, BPT_KIVI_TC_VSLOTS,
+                                    BPT_KIVI_TC_MINB>;
+  const size_t smem = C::smem_bytes(C::CHUNK / kp.d.box_rows);
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) !=
+      cudaSuccess)
+    return BPT_ERR_LAUNCH;
+  dim3 grid(kp.d.splits, kp.d.kv_heads, kp.d.batch);
+  kern<<<grid, C::THREADS, smem, st>>>(tk, tv, tks, tkz, tvs, tvz, kp);
+  return BPT_OK;
+}
+
+template <int FMT>
+int launch_int(const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tks,
+               const CUtensorMap& tkz, const KiviParams& kp, cudaStream_t st) {
+  using C = IntCfg<FMT>;
+  constexpr int kStages = FMT == BPT_KV_INT4 ? BPT_KIVI_INT4_STAGES : BPT_KIVI_INT8_STAGES;
+  auto kern = kivi_int_decode_kernel<FMT, kStages, BPT_KIVI_INT_MINB>;
+  const size_t smem = C::smem_bytes(C::CHUNK / kp.d.box_rows);
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) !=
+      cudaSuccess)
+    return BPT_ERR_LAUNCH;
+  dim3 grid(kp.d.splits, kp.d.kv_heads, kp.d.batch);
+  kern<<<grid, C::THREADS, smem, st>>>(tk, tv, tks, tkz, kp);
+  return BPT_OK;
+}
+
 }  // namespace kivi
 
 // 3-D tiled map over a [num_blocks, H, 128] fp16 parameter array (unit inner stride), box =
@@ -716,6 +802,82 @@ int encode_param_map(CUtensorMap* map, const void* base, int kv_heads, int64_t n
                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? BPT_OK : BPT_ERR_TENSOR_MAP;
+}
+
+// 3-D tiled map over a [num_blocks, block_size, H] fp16 per-token parameter array (v_scale /
+// v_zero), box = 8 heads x box_rows tokens of one block.
+int encode_vparam_map(CUtensorMap* map, const void* base, int kv_heads, int block_size,
+                      int64_t num_blocks, int64_t s_blk, int64_t s_tok, int box_rows) {
+  auto enc = tensor_map_encoder_fn();
+  if (!enc) return BPT_ERR_DRIVER;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || ((s_blk * 2) % 16) || ((s_tok * 2) % 16))
+    return BPT_ERR_ALIGNMENT;
+  cuuint64_t dims[3] = {cuuint64_t(kv_heads), cuuint64_t(block_size),
+                        cuuint64_t(num_blocks > 0 ? num_blocks : 1)};
+  cuuint64_t strides[2] = {cuuint64_t(s_tok * 2), cuuint64_t(s_blk * 2)};
+  cuuint32_t box[3] = {8u, cuuint32_t(box_rows), 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? BPT_OK : BPT_ERR_TENSOR_MAP;
+}
+
+namespace {
+
+int ilog2(int x) {
+  int r = 0;
+  while ((1 << (r + 1)) <= x) ++r;
+  return r;
+}
+
+// Which KIVI kernel serves a (format, group, block_size, kv_heads):
+//   TC   INT8 / INT4, group <= 4, block_size >= 32, kv_heads a multiple of 8 (the per-token
+//        value parameters arrive as TMA boxes of 8 heads): tcgen05 integer MMAs (kivi_tc.cuh)
+//   INT  other INT8 / INT4 with group <= 4: mma.sync integer MMAs (kivi_int.cuh)
+//   F16  FP8, or group > 4: fp16 mma.sync with hi / lo operand pairs (this file)
+// TC and INT share the 128-token chunk, so the split count does not depend on the choice.
+enum class KiviKernel { TC, INT, F16 };
+
+KiviKernel kivi_kernel_for(int format, int group, int block_size, int kv_heads) {
+  if ((format == BPT_KV_INT8 || format == BPT_KV_INT4) && group <= 4)
+    return (block_size >= 32 && kv_heads % 8 == 0) ? KiviKernel::TC : KiviKernel::INT;
+  return KiviKernel::F16;
+}
+
+// tokens per pipeline stage and CTAs per SM of the kernel serving (format, group)
+void kivi_kernel_shape(int format, int group, int block_size, int kv_heads, int* chunk,
+                       int* resident) {
+  using namespace kivi;
+  const bool int4 = format == BPT_KV_INT4;
+  switch (kivi_kernel_for(format, group, block_size, kv_heads)) {
+    case KiviKernel::TC:
+      *chunk = TcCfg<BPT_KV_INT8>::CHUNK;
+      *resident = int4 ? tc_resident_ctas<BPT_KV_INT4>(block_size)
+                       : tc_resident_ctas<BPT_KV_INT8>(block_size);
+      break;
+    case KiviKernel::INT:
+      *chunk = IntCfg<BPT_KV_INT8>::CHUNK;
+      *resident = int4 ? int_resident_ctas<BPT_KV_INT4>(block_size)
+                       : int_resident_ctas<BPT_KV_INT8>(block_size);
+      break;
+    default:
+      *chunk = 16 * kNcw;
+      *resident = BPT_KIVI_MINB;
+  }
+}
+
+}  // namespace
+
+int effective_splits_kivi(int format, int batch, int kv_heads, int q_heads, int block_size,
+                          int max_blocks, int num_splits, int sm_count) {
+  const int group = (kv_heads > 0 && q_heads > 0) ? q_heads / kv_heads : 1;
+  int chunk, resident;
+  kivi_kernel_shape(format, group, block_size, kv_heads, &chunk, &resident);
+  const int s = num_splits > 0 ? num_splits
+                               : plan_splits(batch, kv_heads, block_size, max_blocks, sm_count,
+                                             resident, chunk);
+  return clamp_splits(s, block_size, max_blocks, chunk);
 }
 
 // Launch the KIVI split kernel (final_out: one split writes fp16 out directly).
@@ -749,7 +911,16 @@ int run_split_kivi(const bpt_kivi_cache& c, const void* q, int64_t q_sb, int64_t
 
   KiviParams kp{};
   DecodeParams& p = kp.d;
-  const int chunk = 16 * kNcw;
+  KiviKernel which = kivi_kernel_for(c.format, group, bs, c.kv_heads);
+  // the value-parameter TMA boxes need 16-byte aligned bases and strides
+  if (which == KiviKernel::TC &&
+      ((reinterpret_cast<uintptr_t>(c.v_scale) & 15) ||
+       (reinterpret_cast<uintptr_t>(c.v_zero) & 15) || ((c.v_param_stride[0] * 2) % 16) ||
+       ((c.v_param_stride[1] * 2) % 16)))
+    which = KiviKernel::INT;
+  const int chunk = which == KiviKernel::TC    ? TcCfg<BPT_KV_INT8>::CHUNK
+                    : which == KiviKernel::INT ? IntCfg<BPT_KV_INT8>::CHUNK
+                                               : 16 * kNcw;
   const int box_rows = bs < chunk ? bs : chunk;
   const bool int4 = c.format == BPT_KV_INT4;
   CUtensorMap tk, tv, tks, tkz;
@@ -796,7 +967,26 @@ int run_split_kivi(const bpt_kivi_cache& c, const void* q, int64_t q_sb, int64_t
   kp.v_zero = static_cast<const uint8_t*>(fp8 ? c.v_scale : c.v_zero);
   kp.vps0 = c.v_param_stride[0];
   kp.vps1 = c.v_param_stride[1];
+  kp.lbs = ilog2(bs);
+  kp.lbox = ilog2(box_rows);
   const bool g8 = group > 4;
+  if (which != KiviKernel::F16) {
+    if (which == KiviKernel::TC) {
+      CUtensorMap tvs, tvz;
+      rc = encode_vparam_map(&tvs, c.v_scale, c.kv_heads, bs, c.num_blocks, c.v_param_stride[0],
+                             c.v_param_stride[1], box_rows);
+      if (rc) return rc;
+      rc = encode_vparam_map(&tvz, c.v_zero, c.kv_heads, bs, c.num_blocks, c.v_param_stride[0],
+                             c.v_param_stride[1], box_rows);
+      if (rc) return rc;
+      rc = int4 ? launch_tc<BPT_KV_INT4>(tk, tv, tks, tkz, tvs, tvz, kp, st)
+                : launch_tc<BPT_KV_INT8>(tk, tv, tks, tkz, tvs, tvz, kp, st);
+    } else
+      rc = int4 ? launch_int<BPT_KV_INT4>(tk, tv, tks, tkz, kp, st)
+                : launch_int<BPT_KV_INT8>(tk, tv, tks, tkz, kp, st);
+    if (rc) return rc;
+    return cudaGetLastError() == cudaSuccess ? BPT_OK : BPT_ERR_LAUNCH;
+  }
   switch (c.format) {
     case BPT_KV_INT8:
       rc = g8 ? launch<BPT_KV_INT8, true>(tk, tv, tks, tkz, kp, st)
@@ -830,8 +1020,8 @@ extern "C" int bpt_decode_kivi(const bpt_kivi_cache* cache, const void* q, int64
   if (!workspace || !out) return BPT_ERR_INVALID_ARGUMENT;
   if ((reinterpret_cast<uintptr_t>(out) & 15) || ((o_sb * 2) % 16) || ((o_sh * 2) % 16))
     return BPT_ERR_ALIGNMENT;
-  const int S = bpt_effective_splits(batch, cache->kv_heads, cache->block_size, max_blocks,
-                                     num_splits, sm_count);
+  const int S = effective_splits_kivi(cache->format, batch, cache->kv_heads, q_heads,
+                                      cache->block_size, max_blocks, num_splits, sm_count);
   if (workspace_bytes < bpt_decode_workspace_bytes(batch, q_heads, cache->head_dim, S))
     return BPT_ERR_WORKSPACE_TOO_SMALL;
   WorkspaceView ws = workspace_view(workspace, batch, q_heads, cache->head_dim, S);
@@ -842,6 +1032,13 @@ extern "C" int bpt_decode_kivi(const bpt_kivi_cache* cache, const void* q, int64
   if (rc || S == 1) return rc;
   return launch_merge(ws.o_part, ws.lse, batch, q_heads, S, cache->head_dim,
                       static_cast<__half*>(out), o_sb, o_sh, nullptr, nullptr, st, true);
+}
+
+extern "C" int bpt_effective_splits_kivi(int format, int batch, int kv_heads, int q_heads,
+                                         int block_size, int max_blocks, int num_splits,
+                                         int sm_count) {
+  return effective_splits_kivi(format, batch, kv_heads, q_heads, block_size, max_blocks,
+                               num_splits, sm_count);
 }
 
 extern "C" int bpt_decode_kivi_partial(const bpt_kivi_cache* cache, const void* q, int64_t q_sb,

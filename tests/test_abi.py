@@ -56,6 +56,26 @@ def test_planner_fills_b200():
     assert effective_splits(2, 8, 16, 512, 1, 148) == 1
 
 
+def test_kivi_planner_uses_the_serving_kernels_shape():
+    import ctypes
+    from bpt import _lib
+    f = _lib.register("bpt_effective_splits_kivi", ctypes.c_int, [ctypes.c_int] * 8)
+    INT8, FP8, INT4 = 1, 2, 4 - 1
+    # B=1, 128k tokens, bs=64, group 4: tcgen05 kernel, 128-token stages, 2 CTAs per SM
+    # (148 x 2 / 8 kv heads = 37 splits)
+    assert f(INT4, 1, 8, 32, 64, 2048, 0, 148) == 37
+    assert f(INT8, 1, 8, 32, 64, 2048, 0, 148) == 37
+    # 16-token pages: the mma.sync integer kernel (INT4: 2 CTAs per SM, INT8: 1)
+    assert f(INT4, 1, 8, 32, 16, 8192, 0, 148) == 37
+    assert f(INT8, 1, 8, 32, 16, 8192, 0, 148) == 18
+    # FP8 and group 8 stay on the fp16-MMA kernel: 4 CTAs per SM, 32-token stages
+    assert f(FP8, 1, 8, 32, 64, 2048, 0, 148) == 74
+    assert f(INT4, 1, 8, 64, 64, 2048, 0, 148) == 74
+    # explicit requests are clamped to the 128-token chunk count
+    assert f(INT4, 1, 8, 32, 64, 3, 50, 148) == 2
+    assert f(INT4, 1, 8, 32, 64, 3, 1, 148) == 1
+
+
 def test_workspace_bytes_monotone():
     from bpt.decode import workspace_bytes
     a = workspace_bytes(2, 32, 128, 1)
