@@ -124,14 +124,30 @@ def measured_peaks():
         return FALLBACK_HBM_GBS, "fallback (no MEASURED_PEAKS.json)"
 
 
-def ncu_traffic(workload):
-    """DRAM bytes per launch of the split kernel from a committed ncu summary, if any."""
+def split_kernel_name(fmt, block_size):
+    """The stage-1 kernel a decode call of this format launches (Llama-3-8B head shape)."""
+    if fmt == "fp16":
+        return "split_kv_fp16_mma_kernel"
+    if fmt in ("int8", "int4") and block_size >= 32:   # group 4, 8 kv heads
+        return f"kivi_tc_decode_kernel<{fmt}>"
+    if fmt in ("int8", "int4"):
+        return f"kivi_int_decode_kernel<{fmt}>"
+    return f"kivi_decode_kernel<{fmt}>"
+
+
+def ncu_traffic(kernel, algorithmic_bytes):
+    """DRAM bytes per launch of the stage-1 kernel: the committed ncu ratio (read + write over
+    algorithmic bytes, profiles/dram_traffic.json) scaled to this workload, or (None, None)."""
     path = os.path.join(ROOT, "profiles", "dram_traffic.json")
     try:
         with open(path) as f:
-            d = json.load(f)
-        e = d.get(workload)
-        return (float(e["bytes_per_launch"]), e.get("note")) if e else (None, None)
+            e = json.load(f)["kernels"].get(kernel)
+        if not e:
+            return None, None
+        note = (f"ncu dram__bytes_read.sum + dram__bytes_write.sum of {kernel} on "
+                f"{e['capture_workload']} = {e['ratio']:.5f} x algorithmic bytes, scaled to this "
+                "workload's algorithmic bytes")
+        return float(e["ratio"]) * algorithmic_bytes, note
     except Exception:
         return None, None
 
@@ -500,7 +516,7 @@ def run_bpt(args):
 
     peak, peak_src = measured_peaks()
     achieved_gbs = kernel_bytes / (kern_ms * 1e-3) / 1e9
-    traffic, traffic_note = ncu_traffic(args.workload)
+    traffic, traffic_note = ncu_traffic(split_kernel_name(fmt, bs), kernel_bytes)
     ms_per_step = elapsed_max / args.steps
     line = {
         "metric": metric_name(wl),
@@ -520,8 +536,7 @@ def run_bpt(args):
         "timing": ("eager calls" if (args.eager or seqshard)
                    else "CUDA-graph replay of one product call per step"),
         "roofline": {"bound": "hbm",
-                     "kernel": ("split_kv_fp16_mma_kernel" if fmt == "fp16" else
-                                f"kivi_decode_kernel<{fmt}>")
+                     "kernel": split_kernel_name(fmt, bs)
                                + " (+ PDL-chained merge_splits_kernel; timed together per call)",
                      "achieved": achieved_gbs, "peak": peak, "unit": "GB/s",
                      "frac": achieved_gbs / peak, "peak_source": peak_src,
