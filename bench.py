@@ -67,7 +67,10 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", choices=["bpt", "reference"], default="bpt")
+    ap.add_argument("--impl", choices=["bpt", "reference", "reference-triton"], default="bpt",
+                    help="reference: the reference's CPU algorithm (numpy port) on the host "
+                         "cores; reference-triton: the reference's own Triton FP16 kernel "
+                         "(installed under baseline/_ref) on this GPU, same inputs")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--no-e2e", action="store_true")
@@ -552,10 +555,101 @@ def run_bpt(args):
     return 0
 
 
+# ----------------------------------------------------------------------------- reference Triton arm
+
+def load_reference_triton():
+    """The reference's src/bpt/triton_fp16.py from its offline install under baseline/_ref,
+    loaded as a standalone module (the installed package is also called `bpt`)."""
+    import importlib.util
+    path = os.path.join(ROOT, "baseline", "_ref", "bpt", "triton_fp16.py")
+    if not os.path.exists(path):
+        return None, "reference not installed under baseline/_ref"
+    spec = importlib.util.spec_from_file_location("bpt_reference_triton_fp16", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod, None
+
+
+def run_reference_triton(args):
+    """--impl reference-triton: the reference's paged_decode_attention_triton
+    (src/bpt/triton_fp16.py:183-247) on this GPU over the same seeded workload as the bpt arm,
+    timed per call with CUDA events (eager: the reference syncs on seq_lens.min() every call,
+    so it cannot be captured in a CUDA graph). Single GPU; FP16 only (the reference has no
+    quantized path). Also reports the best fixed num_splits and the max abs difference between
+    its output and bpt's on the same inputs."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    wl = WORKLOADS[args.workload]
+    base = {"impl": "reference-triton", "metric": metric_name(wl),
+            "config": config_dict(args.workload, wl, 1)}
+    if wl["fmt"] != "fp16":
+        print(json.dumps({**base, "unavailable": "the reference has no quantized KV kernel"}))
+        return 0
+    import torch
+    ref, why = load_reference_triton()
+    if ref is None:
+        print(json.dumps({**base, "unavailable": why}))
+        return 0
+    from bpt import decode as dec
+    from bpt.cache import random_paged_workload
+    from bpt.roofline import decode_call_bytes
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    bs = wl["block_size"]
+    lens = workload_lens(wl, 0, args.seed)
+    w = random_paged_workload(lens, HQ, HKV, D, bs, dev, seed=args.seed, spare_blocks=64)
+    q, kc, vc, bt, sl = w["q"], w["k_cache"], w["v_cache"], w["block_table"], w["seq_lens"]
+    nbytes = decode_call_bytes(lens, bs, HQ, HKV, D, "fp16")
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(num_splits, steps, warmup):
+        f = lambda: ref.paged_decode_attention_triton(q, kc, vc, bt, sl, num_splits=num_splits)
+        for _ in range(warmup):
+            f()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            f()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    ms = timed(None, args.steps, args.warmup)
+    best = None
+    for s in (1, 2, 4, 8, 16, 32, 64, 128):
+        m = timed(s, max(3, args.steps // 4), 2)
+        if best is None or m < best[1]:
+            best = (s, m)
+    out_ref = ref.paged_decode_attention_triton(q, kc, vc, bt, sl)
+    out_bpt = dec.paged_decode_attention(q, kc, vc, bt, sl)
+    torch.cuda.synchronize()
+    diff = (out_ref.float() - out_bpt.float()).abs().max().item()
+    peak, peak_src = measured_peaks()
+    tbps = nbytes / (ms * 1e-3) / 1e12
+    line = {
+        **base, "value": tbps, "unit": "TB/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic (same seeded inputs as bpt)",
+        "timing": "eager calls, CUDA events around K calls (the reference host-syncs per call)",
+        "splits": "reference heuristic choose_num_splits",
+        "frac_of_measured_hbm": tbps * 1e3 / peak, "peak_source": peak_src,
+        "best_fixed_split": {"num_splits": best[0], "ms_per_step": best[1],
+                             "value": nbytes / (best[1] * 1e-3) / 1e12},
+        "max_abs_diff_vs_bpt": diff,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.impl == "reference-triton":
+        return run_reference_triton(args)
     return run_bpt(args)
 
 

@@ -207,6 +207,12 @@ int bpt_decode_fp16_noalloc(const void* q, int64_t q_sb, int64_t q_sh,
                             int block_size, int max_blocks,
                             float scale, int num_splits, int sm_count, void* stream);
 
+/* Self-test of failure detection: launches one CTA that waits on a pipeline barrier nothing
+ * completes, with a budget of budget_us microseconds (1 .. 1e6), on the decode kernels' own
+ * bounded-wait code; it must give up and OR BPT_DEV_WAIT_TIMEOUT into *status (device
+ * memory), leaving the CUDA context usable. No reference counterpart. */
+int bpt_selftest_wait_timeout(unsigned* status, unsigned budget_us, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -69,6 +69,7 @@ _SIGNATURES = [
      [c_vp, c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_i64, c_i64, c_vp]),
     ("bpt_merge_states", c_i32,
      [c_vp, c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp]),
+    ("bpt_selftest_wait_timeout", c_i32, [c_vp, ctypes.c_uint, c_vp]),
 ]
 
 # Status codes (include/bpt.h enum bpt_status)

@@ -74,15 +74,19 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
   return ok != 0;
 }
 
-// Wait for the phase with the given parity to complete. Returns false if the time budget ran
-// out (the caller records BPT_DEV_WAIT_TIMEOUT and leaves the pipeline).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// Wait for the phase with the given parity to complete, giving up after budget_ns. Returns
+// false if the budget ran out (the caller records BPT_DEV_WAIT_TIMEOUT and leaves the pipeline).
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, uint64_t budget_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   while (true) {
     if (mbar_try_wait_sleep(bar, parity, 1000000u)) return true;
-    if (global_timer_ns() - t0 > kWaitBudgetNs) return false;
+    if (global_timer_ns() - t0 > budget_ns) return false;
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  return mbar_wait_for(bar, parity, kWaitBudgetNs);
 }
 
 // ----------------------------------------------------------------------------- TMA

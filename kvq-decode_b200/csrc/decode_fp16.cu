@@ -413,8 +413,13 @@ merge_splits_kernel(const float* __restrict__ o_part, const float* __restrict__ 
                     const MergeLayout lay, int q_heads, int splits, int D,
                     __half* __restrict__ out16, int64_t o_sb, int64_t o_sh,
                     float* __restrict__ o32, float* __restrict__ lse32) {
+  // One CTA per (q head, sequence). The S partial rows are spread over the 4 warps (warp w
+  // takes splits w, w + 4, ...) and each lane holds 4 consecutive channels, so a warp keeps
+  // several independent 16-byte loads in flight instead of walking the splits one dependent
+  // load at a time; the 4 warp sums are added through shared memory.
   extern __shared__ float w_s[];  // [splits]
   __shared__ float red[4];
+  __shared__ float4 part[4][64];  // per-warp sums, D <= 256
   const int hq = blockIdx.x, b = blockIdx.y;
   const float* l = lse + int64_t(b) * lay.l_sb + int64_t(hq) * lay.l_sh;
   const float* o = o_part + int64_t(b) * lay.o_sb + int64_t(hq) * lay.o_sh;
@@ -440,17 +445,60 @@ merge_splits_kernel(const float* __restrict__ o_part, const float* __restrict__ 
   if (lane == 0) red[warp] = wsum;
   __syncthreads();
   const float W = red[0] + red[1] + red[2] + red[3];
-  for (int d = tid; d < D; d += blockDim.x) {
-    float a = 0.f;
-    for (int s = 0; s < splits; ++s) {
-      const float w = w_s[s];
-      if (w != 0.f) a = fmaf(w, o[s * lay.o_ss + d], a);
-    }
-    const float r = W > 0.f ? a / W : 0.f;
+  const float invW = W > 0.f ? 1.f / W : 0.f;
+  auto put = [&](int d, float a) {
+    const float r = W > 0.f ? a * invW : 0.f;
     if constexpr (F16OUT) {
       out16[int64_t(b) * o_sb + int64_t(hq) * o_sh + d] = __float2half_rn(r);
     } else {
       o32[(int64_t(b) * q_heads + hq) * D + d] = r;
+    }
+  };
+  // a split of weight 0 contributes nothing even if its row holds garbage (select, not branch,
+  // so the loads stay independent)
+  const bool vec = (D % 4 == 0) && D <= 256 && (lay.o_ss % 4 == 0) &&
+                   ((reinterpret_cast<uintptr_t>(o) & 15) == 0);
+  if (vec) {
+    const int nd4 = D >> 2;
+    for (int c = lane; c < nd4; c += 32) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      auto add = [&](int s) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(o + s * lay.o_ss) + c);
+        const float w = w_s[s];
+        const bool on = w != 0.f;
+        acc.x = fmaf(w, on ? v.x : 0.f, acc.x);
+        acc.y = fmaf(w, on ? v.y : 0.f, acc.y);
+        acc.z = fmaf(w, on ? v.z : 0.f, acc.z);
+        acc.w = fmaf(w, on ? v.w : 0.f, acc.w);
+      };
+      int s = warp;
+      for (; s + 12 < splits; s += 16) {
+        add(s);
+        add(s + 4);
+        add(s + 8);
+        add(s + 12);
+      }
+      for (; s < splits; s += 4) add(s);
+      part[warp][c] = acc;
+    }
+    __syncthreads();
+    for (int c = tid; c < nd4; c += blockDim.x) {
+      const float4 a0 = part[0][c], a1 = part[1][c], a2 = part[2][c], a3 = part[3][c];
+      put(4 * c + 0, (a0.x + a1.x) + (a2.x + a3.x));
+      put(4 * c + 1, (a0.y + a1.y) + (a2.y + a3.y));
+      put(4 * c + 2, (a0.z + a1.z) + (a2.z + a3.z));
+      put(4 * c + 3, (a0.w + a1.w) + (a2.w + a3.w));
+    }
+  } else {
+    for (int d = tid; d < D; d += blockDim.x) {
+      float a = 0.f;
+#pragma unroll 8
+      for (int s = 0; s < splits; ++s) {
+        const float w = w_s[s];
+        const float v = o[s * lay.o_ss + d];
+        a = fmaf(w, w != 0.f ? v : 0.f, a);
+      }
+      put(d, a);
     }
   }
   if constexpr (!F16OUT) {

@@ -162,6 +162,26 @@ def test_device_check_flags_bad_block_id(monkeypatch):
     dec.paged_decode_attention(q, kc, vc, bt, sl)  # clean call passes in checked mode
 
 
+def test_bounded_wait_gives_up_and_reports_timeout():
+    """Failure detection without a fault: a CTA waits (through the decode kernels' bounded
+    wait) on a barrier phase nothing completes; after its 50 ms budget it must return and
+    report BPT_DEV_WAIT_TIMEOUT in the status word, and the context must stay usable."""
+    import time
+    from bpt import _lib, paged_decode_attention
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    t0 = time.perf_counter()
+    rc = _lib.lib().bpt_selftest_wait_timeout(status.data_ptr(), 50000, stream)
+    _lib.check(rc, "bpt_selftest_wait_timeout")
+    torch.cuda.synchronize()
+    waited = time.perf_counter() - t0
+    assert int(status.item()) & 4, "BPT_DEV_WAIT_TIMEOUT not reported"
+    assert 0.04 < waited < 5.0, waited
+    _, c = _case("c1")
+    out = paged_decode_attention(*_to_gpu(c))           # the context still works
+    assert_close(out.cpu().numpy(), golden_arrays()["c1/out"], what="after the timeout")
+
+
 def torch_reference(q, k_cache, v_cache, block_table, seq_lens, scale=None):
     """fp32 torch restatement of reference.py:20-49 on the GPU (large cases only)."""
     B, Hq, D = q.shape
