@@ -80,6 +80,8 @@ def parse():
     ap.add_argument("--eager", action="store_true",
                     help="time eager calls instead of CUDA-graph replays of the call")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--splits", type=int, default=0,
+                    help="force the split count per sequence (0: the planner's choice)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="budget of the CPU-baseline sample")
     return ap.parse_args()
@@ -381,10 +383,10 @@ def run_bpt(args):
     max_blocks = bt.shape[1]
     sms = dec._sm_count(local)
     if wl["fmt"] == "fp16":
-        S = dec.effective_splits(B, HKV, bs, max_blocks, None, sms)
+        S = dec.effective_splits(B, HKV, bs, max_blocks, args.splits or None, sms)
     else:
         from bpt.quant import effective_splits_kivi
-        S = effective_splits_kivi(kvcache, B, HQ, max_blocks, None, sms)
+        S = effective_splits_kivi(kvcache, B, HQ, max_blocks, args.splits or None, sms)
     # algorithmic bytes of this rank's share of the job (seqshard: its tokens of the sequences,
     # plus q/out once on rank 0 so the job total counts them once)
     step_bytes = decode_call_bytes(lens, bs, HQ, HKV, D, wl["fmt"])
@@ -404,10 +406,10 @@ def run_bpt(args):
                                     vc if fmt == "fp16" else None, bt, sl, out=out,
                                     kivi_cache=None if fmt == "fp16" else kvcache)
         elif fmt == "fp16":
-            dec.paged_decode_attention(q, kc, vc, bt, sl, out=out, workspace=ws)
+            dec.paged_decode_attention(q, kc, vc, bt, sl, num_splits=S, out=out, workspace=ws)
         else:
             from bpt.quant import paged_decode_attention_kivi
-            paged_decode_attention_kivi(q, kvcache, bt, sl, out=out, workspace=ws)
+            paged_decode_attention_kivi(q, kvcache, bt, sl, num_splits=S, out=out, workspace=ws)
 
     # The device-timed leg replays the call as a CUDA graph (what a serving engine does with a
     # decode step), so host-side Python cost does not leak into small workloads' timing.
