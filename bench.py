@@ -76,7 +76,10 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--seqshard", action="store_true",
                     help="shard every sequence's tokens over the ranks (strong scaling; the "
-                         "partial softmax states are merged with one NCCL all-gather)")
+                         "ranks exchange their partial softmax states)")
+    ap.add_argument("--exchange", choices=["nvlink", "nccl"], default="nvlink",
+                    help="sequence sharding: fused NVLink peer-store kernel (default) or one "
+                         "NCCL all-gather")
     ap.add_argument("--eager", action="store_true",
                     help="time eager calls instead of CUDA-graph replays of the call")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -100,7 +103,7 @@ def config_index(wl):
     return 4 if wl["fmt"] == "int4" else 3
 
 
-def config_dict(name, wl, n_gpus, seqshard=False):
+def config_dict(name, wl, n_gpus, seqshard=False, exchange="nvlink"):
     return {
         "workload": f"{name}: BASELINE configs[{config_index(wl)}] "
                     f"{wl['fmt']} paged KV, Llama-3-8B layer (Hq={HQ}, Hkv={HKV}, D={D}), "
@@ -113,7 +116,9 @@ def config_dict(name, wl, n_gpus, seqshard=False):
         "kv_dtype": wl["fmt"], "batch_per_gpu": wl["batch"], "ctx": wl["ctx"],
         "block_size": wl["block_size"], "q_heads": HQ, "kv_heads": HKV, "head_dim": D,
         "parallelism": (f"sequence-sharded x{n_gpus} (page-aligned token ranges per rank, "
-                        f"partial softmax states merged after one NCCL all-gather)"
+                        + ("partial softmax states exchanged by one fused kernel storing into "
+                           "the peers' memory over NVLink)" if exchange == "nvlink" else
+                           "partial softmax states merged after one NCCL all-gather)")
                         if seqshard else
                         f"batch-sharded x{n_gpus} (independent sequences per rank)"),
         "l2": "no flush: per-step working set (GBs of KV) far exceeds the 126 MB L2",
@@ -396,7 +401,13 @@ def run_bpt(args):
     kernel_bytes = step_bytes
     out = torch.empty_like(q)
     ws = torch.empty(dec.workspace_bytes(B, HQ, D, S), dtype=torch.uint8, device=dev)
-    launches_per_step = (2 if S > 1 else 1) + (2 if seqshard else 0)  # + state merge kernels
+    ex = None
+    if seqshard and args.exchange == "nvlink":
+        from bpt.dist import SequenceShardExchange
+        ex = SequenceShardExchange(B, HQ, D)
+    # split kernel (+ PDL merge); sequence sharding: split + fused exchange, or split + state
+    # merge + NCCL all-gather + rank merge
+    launches_per_step = ((2 if ex is not None else 4) if seqshard else (2 if S > 1 else 1))
     stream = torch.cuda.current_stream(dev)
 
     def call():
@@ -404,7 +415,7 @@ def run_bpt(args):
         if seqshard:
             decode_sequence_sharded(q, kc if fmt == "fp16" else None,
                                     vc if fmt == "fp16" else None, bt, sl, out=out,
-                                    kivi_cache=None if fmt == "fp16" else kvcache)
+                                    kivi_cache=None if fmt == "fp16" else kvcache, exchange=ex)
         elif fmt == "fp16":
             dec.paged_decode_attention(q, kc, vc, bt, sl, num_splits=S, out=out, workspace=ws)
         else:
@@ -414,7 +425,7 @@ def run_bpt(args):
     # The device-timed leg replays the call as a CUDA graph (what a serving engine does with a
     # decode step), so host-side Python cost does not leak into small workloads' timing.
     graph = None
-    if not args.eager and not seqshard:  # sequence sharding includes an NCCL collective: eager
+    if not args.eager and not (seqshard and ex is None):  # an NCCL all-gather step: eager
         call()
         torch.cuda.synchronize()
         side = torch.cuda.Stream(dev)
@@ -425,6 +436,8 @@ def run_bpt(args):
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
             call()
+
+    graph_used = graph is not None
 
     def step(ev_a=None, ev_b=None):
         if ev_a is not None:
@@ -514,7 +527,10 @@ def run_bpt(args):
 
     graph = None
     if world > 1:
+        torch.cuda.synchronize()
         dist.barrier(device_ids=[local])
+        if ex is not None:
+            ex.close()
         dist.destroy_process_group()
     if rank != 0:
         return 0
@@ -533,12 +549,12 @@ def run_bpt(args):
                            "(A100-80GB, B=32 ctx=16k, docs/NOTES.md:99)",
         "dtype": "f16" if fmt == "fp16" else f"{fmt} KV codes, f16 q/out, f32 math",
         "data": "synthetic (seeded N(0,1) fp16 q/K/V, random block tables)",
-        "config": config_dict(args.workload, wl, world, seqshard),
+        "config": config_dict(args.workload, wl, world, seqshard, args.exchange),
         "pct_of_b200_spec_peak": 100.0 * value_tbps * 1e3 / (B200_SPEC_GBS * world),
         "us_per_decode_step": {"one_layer": ms_per_step * 1e3,
                                "llama3_8b_32_layers": ms_per_step * 1e3 * 32},
         "splits": S,
-        "timing": ("eager calls" if (args.eager or seqshard)
+        "timing": ("eager calls" if graph_used is False
                    else "CUDA-graph replay of one product call per step"),
         "roofline": {"bound": "hbm",
                      "kernel": split_kernel_name(fmt, bs)

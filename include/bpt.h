@@ -207,6 +207,30 @@ int bpt_decode_fp16_noalloc(const void* q, int64_t q_sb, int64_t q_sh,
                             int block_size, int max_blocks,
                             float scale, int num_splits, int sm_count, void* stream);
 
+/* ---------------------------------------------------------------- sequence sharding
+ *
+ * Fused cross-GPU exchange for sequence-sharded decode (one process per GPU of one node; no
+ * reference counterpart). Each rank allocates one receive buffer with bpt_seqx_alloc, sends
+ * its IPC handle to the others (any out-of-band channel, e.g. an all-gather of the 64 bytes),
+ * and maps theirs with bpt_seqx_open. Per call, after the split kernel wrote this rank's
+ * partial states (bpt_decode_fp16_partial / bpt_decode_kivi_partial into o_part [B, Hq, S, D],
+ * lse [B, Hq, S]), bpt_seqx_merge_fp16 merges the splits, stores the per-(sequence, q head)
+ * state into every rank's buffer over NVLink (peer stores, no collective library), waits
+ * (time-bounded, budget_us) for all ranks' states and writes the merged fp16 out [B, Hq, D] on
+ * every rank. bufs[r] is rank r's buffer as mapped in this process (bufs[rank] = own). All
+ * ranks must make the same sequence of calls with the same batch / q_heads / head_dim; a wait
+ * that runs out sets BPT_DEV_WAIT_TIMEOUT in *status. head_dim % 4 == 0, <= 256; world <= 8. */
+#define BPT_IPC_HANDLE_BYTES 64
+size_t bpt_seqx_buffer_bytes(int world, int batch, int q_heads, int head_dim);
+int bpt_seqx_alloc(size_t bytes, void** buf, void* ipc_handle);
+int bpt_seqx_open(const void* ipc_handle, void** peer_buf);
+int bpt_seqx_close(void* peer_buf);
+int bpt_seqx_free(void* buf);
+int bpt_seqx_merge_fp16(const float* o_part, const float* lse, int batch, int q_heads,
+                        int head_dim, int splits, void* const* bufs, int world, int rank,
+                        void* out, int64_t o_sb, int64_t o_sh, unsigned* status,
+                        unsigned budget_us, void* stream);
+
 /* Self-test of failure detection: launches one CTA that waits on a pipeline barrier nothing
  * completes, with a budget of budget_us microseconds (1 .. 1e6), on the decode kernels' own
  * bounded-wait code; it must give up and OR BPT_DEV_WAIT_TIMEOUT into *status (device

@@ -2,7 +2,9 @@
 
 * sequence sharding: every rank holds only its page-aligned token range of each sequence
   (FP16 and INT4 KIVI caches); decode_sequence_sharded (local split-KV + state merge + one
-  all_gather_into_tensor + rank-state merge) must equal the single-GPU result;
+  all_gather_into_tensor + rank-state merge) must equal the single-GPU result, and so must the
+  fused NVLink exchange (SequenceShardExchange: split kernel + one peer-store kernel), over
+  repeated calls and CUDA-graph replays;
 * batch sharding: each rank decodes its own sequences; gather_outputs equals single-GPU.
 """
 import datetime
@@ -31,8 +33,8 @@ def _worker(rank, world, port, result_dir):
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path[:0] = [root, os.path.join(root, "kvq-decode_b200")]
     from bpt import paged_decode_attention
-    from bpt.dist import decode_batch_sharded, decode_sequence_sharded, gather_outputs, \
-        shard_range, token_shards
+    from bpt.dist import SequenceShardExchange, decode_batch_sharded, \
+        decode_sequence_sharded, gather_outputs, shard_range, token_shards
     from bpt.quant import empty_kivi_cache, paged_decode_attention_kivi, quantize_append
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
@@ -84,6 +86,32 @@ def _worker(rank, world, port, result_dir):
                                                                device=dev))
     errs["fp16_seq"] = (out.float() - ref.float()).abs().max().item()
 
+    # ---------------- the same through the fused NVLink exchange (eager, then graph replays)
+    ex = SequenceShardExchange(B, Hq, D)
+    fused = None
+    for _ in range(3):
+        fused = decode_sequence_sharded(q, kc, vc, bt, sl, exchange=ex)
+    torch.cuda.synchronize()
+    errs["fp16_seq_fused"] = (fused.float() - ref.float()).abs().max().item()
+    errs["fused_vs_nccl"] = (fused.float() - out.float()).abs().max().item()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    gout = torch.empty_like(fused)
+    with torch.cuda.stream(side):
+        decode_sequence_sharded(q, kc, vc, bt, sl, exchange=ex, out=gout)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            decode_sequence_sharded(q, kc, vc, bt, sl, exchange=ex, out=gout)
+    torch.cuda.synchronize()
+    for _ in range(4):
+        gout.zero_()
+        graph.replay()
+    torch.cuda.synchronize()
+    errs["fp16_seq_fused_graph"] = (gout.float() - ref.float()).abs().max().item()
+    errs["fused_status"] = float(ex.status.item())
+    del graph
+    ex.close()
+
     # ---------------- INT4 KIVI sequence sharding (page-aligned shards -> identical codes)
     bs = 64
     lens = [40000, 130]
@@ -120,6 +148,11 @@ def _worker(rank, world, port, result_dir):
     c_full, bt_full, sl_full = kivi_cache(k, v, lens, 7)
     ref = paged_decode_attention_kivi(q, c_full, bt_full, sl_full)
     errs["int4_seq"] = (out.float() - ref.float()).abs().max().item()
+    ex = SequenceShardExchange(B, Hq, D)
+    fused = decode_sequence_sharded(q, None, None, bt_loc, sl_loc, kivi_cache=c_loc, exchange=ex)
+    torch.cuda.synchronize()
+    errs["int4_seq_fused"] = (fused.float() - ref.float()).abs().max().item()
+    ex.close()
 
     # ---------------- FP16 batch sharding
     Bt, bs = 4 * world, 16
@@ -151,5 +184,7 @@ def test_sharded_decode_matches_single_gpu(tmp_path):
     errs = np.load(tmp_path / "errs.npy", allow_pickle=True).item()
     # split boundaries differ (per-rank splits + rank merge) -> fp32 rounding only
     assert errs["fp16_seq"] < 2e-3, errs
-    assert errs["int4_seq"] < 2e-3, errs
+    assert errs["fp16_seq_fused"] < 2e-3 and errs["fp16_seq_fused_graph"] < 2e-3, errs
+    assert errs["fused_vs_nccl"] < 1e-3 and errs["fused_status"] == 0, errs
+    assert errs["int4_seq"] < 2e-3 and errs["int4_seq_fused"] < 2e-3, errs
     assert errs["fp16_batch"] < 2e-3, errs
