@@ -159,6 +159,7 @@ split_kv_fp16_kernel(const __grid_constant__ CUtensorMap tmK,
     fence_mbar_init();
   }
   __syncthreads();
+  pdl_launch_dependents();   // the merge grid may launch now; it waits for this grid's end
 
   if (warp == kConsumerWarps) {
     // ------------------------------------------------------------------ producer warp
@@ -472,11 +473,13 @@ merge_splits_kernel(const float* __restrict__ o_part, const float* __restrict__ 
         acc.w = fmaf(w, on ? v.w : 0.f, acc.w);
       };
       int s = warp;
+      for (; s + 28 < splits; s += 32) {
+#pragma unroll
+        for (int u = 0; u < 32; u += 4) add(s + u);
+      }
       for (; s + 12 < splits; s += 16) {
-        add(s);
-        add(s + 4);
-        add(s + 8);
-        add(s + 12);
+#pragma unroll
+        for (int u = 0; u < 16; u += 4) add(s + u);
       }
       for (; s < splits; s += 4) add(s);
       part[warp][c] = acc;

@@ -218,6 +218,7 @@ kivi_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
     fence_mbar_init();
   }
   __syncthreads();
+  pdl_launch_dependents();   // the merge grid may launch now; it waits for this grid's end
 
   if (warp == NCW) {
     // ------------------------------------------------------------------ producer warp

@@ -200,6 +200,7 @@ kivi_int_decode_kernel(const __grid_constant__ CUtensorMap tmK,
     qv[0] = f01.x; qv[1] = f01.y; qv[2] = f23.x; qv[3] = f23.y;
   }
   __syncthreads();
+  pdl_launch_dependents();   // the merge grid may launch now; it waits for this grid's end
 
   // ------------------------------------------------------------------ loads of one stage
   const int32_t* bt = p.block_table + int64_t(b) * p.bt_sb;

@@ -272,6 +272,8 @@ kivi_tc_decode_kernel(const __grid_constant__ CUtensorMap tmK,
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
+  // the merge grid may start launching now; it waits for this whole grid to complete
+  pdl_launch_dependents();
   const uint32_t tmem = *tslot;
   const uint32_t pv_col = C::pv_col(nslot);
   int qk_issued = 0, pv_issued = 0;   // MMA warp

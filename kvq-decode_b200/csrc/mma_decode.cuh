@@ -175,6 +175,9 @@ split_kv_fp16_mma_kernel(const __grid_constant__ CUtensorMap tmK,
     fence_mbar_init();
   }
   __syncthreads();
+  // the merge grid may start launching now (it waits in griddepcontrol.wait for this whole
+  // grid to complete), which takes its launch latency off the end of the call
+  pdl_launch_dependents();
 
   if (warp == NCW) {
     // ------------------------------------------------------------------ producer warp
