@@ -83,6 +83,10 @@ def parse():
     ap.add_argument("--eager", action="store_true",
                     help="time eager calls instead of CUDA-graph replays of the call")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=1,
+                    help="decode L independent layers (own KV cache, q, table each) per step, "
+                         "captured in one CUDA graph: L=32 is a whole Llama-3-8B decode step's "
+                         "attention")
     ap.add_argument("--splits", type=int, default=0,
                     help="force the split count per sequence (0: the planner's choice)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
@@ -381,6 +385,19 @@ def run_bpt(args):
                                  spare_blocks=64)
         kvcache = w["cache"]
     q, bt, sl = w["q"], w["block_table"], w["seq_lens"]
+    L = max(1, args.layers)
+    if L > 1 and seqshard:
+        raise SystemExit("--layers > 1 is not combined with --seqshard")
+    extra = []   # layers 1 .. L-1: their own caches, queries, tables and outputs
+    for li in range(1, L):
+        if fmt == "fp16":
+            wx = random_paged_workload(lens, HQ, HKV, D, bs, dev, seed=args.seed + rank + 1009 * li,
+                                       spare_blocks=64)
+        else:
+            wx = random_kivi_workload(lens, HQ, HKV, D, bs, fmt, dev,
+                                      seed=args.seed + rank + 1009 * li, spare_blocks=64)
+        wx["out"] = torch.empty_like(wx["q"])
+        extra.append(wx)
     if seqshard:  # every rank decodes the same queries against its own token shard
         q = torch.randn(q.shape, generator=torch.Generator(device=dev).manual_seed(args.seed),
                         device=dev).to(torch.float16)
@@ -394,7 +411,7 @@ def run_bpt(args):
         S = effective_splits_kivi(kvcache, B, HQ, max_blocks, args.splits or None, sms)
     # algorithmic bytes of this rank's share of the job (seqshard: its tokens of the sequences,
     # plus q/out once on rank 0 so the job total counts them once)
-    step_bytes = decode_call_bytes(lens, bs, HQ, HKV, D, wl["fmt"])
+    step_bytes = decode_call_bytes(lens, bs, HQ, HKV, D, wl["fmt"]) * L
     if seqshard and rank != 0:
         step_bytes -= len(lens) * HQ * D * 2 * 2
     f = KIVI_FORMATS[wl["fmt"]]
@@ -407,7 +424,7 @@ def run_bpt(args):
         ex = SequenceShardExchange(B, HQ, D)
     # split kernel (+ PDL merge); sequence sharding: split + fused exchange, or split + state
     # merge + NCCL all-gather + rank merge
-    launches_per_step = ((2 if ex is not None else 4) if seqshard else (2 if S > 1 else 1))
+    launches_per_step = ((2 if ex is not None else 4) if seqshard else (2 if S > 1 else 1)) * L
     stream = torch.cuda.current_stream(dev)
 
     def call():
@@ -418,9 +435,17 @@ def run_bpt(args):
                                     kivi_cache=None if fmt == "fp16" else kvcache, exchange=ex)
         elif fmt == "fp16":
             dec.paged_decode_attention(q, kc, vc, bt, sl, num_splits=S, out=out, workspace=ws)
+            for wx in extra:   # the layers run in order on one stream and share the workspace
+                dec.paged_decode_attention(wx["q"], wx["k_cache"], wx["v_cache"],
+                                           wx["block_table"], wx["seq_lens"], num_splits=S,
+                                           out=wx["out"], workspace=ws)
         else:
             from bpt.quant import paged_decode_attention_kivi
             paged_decode_attention_kivi(q, kvcache, bt, sl, num_splits=S, out=out, workspace=ws)
+            for wx in extra:
+                paged_decode_attention_kivi(wx["q"], wx["cache"], wx["block_table"],
+                                            wx["seq_lens"], num_splits=S, out=wx["out"],
+                                            workspace=ws)
 
     # The device-timed leg replays the call as a CUDA graph (what a serving engine does with a
     # decode step), so host-side Python cost does not leak into small workloads' timing.
@@ -491,13 +516,23 @@ def run_bpt(args):
         bt_h = bt.cpu().pin_memory()
         sl_h = sl.cpu().pin_memory()
         out_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+        # every layer's q / table / lengths in, every layer's output back
+        ex_h = [(wx["q"].cpu().pin_memory(), wx["block_table"].cpu().pin_memory(),
+                 wx["seq_lens"].cpu().pin_memory(),
+                 torch.empty(wx["out"].shape, dtype=torch.float16).pin_memory()) for wx in extra]
 
         def e2e_step():
             q.copy_(q_h, non_blocking=True)
             bt.copy_(bt_h, non_blocking=True)
             sl.copy_(sl_h, non_blocking=True)
+            for wx, (qx, btx, slx, _) in zip(extra, ex_h):
+                wx["q"].copy_(qx, non_blocking=True)
+                wx["block_table"].copy_(btx, non_blocking=True)
+                wx["seq_lens"].copy_(slx, non_blocking=True)
             call()
             out_h.copy_(out, non_blocking=True)
+            for wx, (_, _, _, ox) in zip(extra, ex_h):
+                ox.copy_(wx["out"], non_blocking=True)
 
         for _ in range(max(args.warmup, 1)):
             e2e_step()
@@ -514,8 +549,8 @@ def run_bpt(args):
         if world > 1:
             dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
         e2e = {"value": bytes_all / (float(e_ms.item()) * 1e-3) / 1e12, "unit": "TB/s",
-               "h2d_bytes_per_step": q.nbytes + bt.nbytes + sl.nbytes,
-               "d2h_bytes_per_step": out.nbytes,
+               "h2d_bytes_per_step": (q.nbytes + bt.nbytes + sl.nbytes) * L,
+               "d2h_bytes_per_step": out.nbytes * L,
                "ms_per_step": float(e_ms.item()) / args.steps,
                "note": "public API bpt.paged_decode_attention; KV cache resident in HBM"}
 
@@ -549,10 +584,13 @@ def run_bpt(args):
                            "(A100-80GB, B=32 ctx=16k, docs/NOTES.md:99)",
         "dtype": "f16" if fmt == "fp16" else f"{fmt} KV codes, f16 q/out, f32 math",
         "data": "synthetic (seeded N(0,1) fp16 q/K/V, random block tables)",
-        "config": config_dict(args.workload, wl, world, seqshard, args.exchange),
+        "config": dict(config_dict(args.workload, wl, world, seqshard, args.exchange),
+                       layers_per_step=L),
         "pct_of_b200_spec_peak": 100.0 * value_tbps * 1e3 / (B200_SPEC_GBS * world),
-        "us_per_decode_step": {"one_layer": ms_per_step * 1e3,
-                               "llama3_8b_32_layers": ms_per_step * 1e3 * 32},
+        "us_per_decode_step": {"one_layer": ms_per_step * 1e3 / L,
+                               "llama3_8b_32_layers": ms_per_step * 1e3 * 32 / L,
+                               "layers_per_step": L,
+                               "32_layers": "measured" if L == 32 else f"{L} measured x {32 / L:g}"},
         "splits": S,
         "timing": ("eager calls" if graph_used is False
                    else "CUDA-graph replay of one product call per step"),
