@@ -182,6 +182,25 @@ def test_bounded_wait_gives_up_and_reports_timeout():
     assert_close(out.cpu().numpy(), golden_arrays()["c1/out"], what="after the timeout")
 
 
+@pytest.mark.parametrize("D", [16, 32, 64, 128, 256])
+@pytest.mark.parametrize("Hq,Hkv", [(8, 8), (16, 8), (32, 8), (16, 2)])   # groups 1, 2, 4, 8
+@pytest.mark.parametrize("bs", [16, 256])
+def test_head_dims_groups_and_page_sizes(D, Hq, Hkv, bs):
+    """Every head_dim the kernels are built for (CUDA-core kernel for 16/32, tensor-core for
+    64/128/256) x groups 1-8 x the smallest and largest page size, ragged lengths with a
+    one-token and a page-crossing sequence, against the numpy oracle."""
+    from bpt import paged_decode_attention
+    from oracle import attention as oa
+    from oracle import cache as oc
+    lens = [1, bs + 3, 3 * bs - 1]
+    c = oc.fp16_case(100 + D + Hq + bs, lens, Hq, Hkv, D, bs, "reference", 8)
+    ref = oa.paged_decode_attention_ref(c["q"], c["k_cache"], c["v_cache"], c["block_table"],
+                                        c["seq_lens"])
+    for ns in (1, 3, None):
+        out = paged_decode_attention(*_to_gpu(c), num_splits=ns)
+        assert_close(out.cpu().numpy(), ref, what=f"D={D} Hq={Hq} Hkv={Hkv} bs={bs} ns={ns}")
+
+
 def torch_reference(q, k_cache, v_cache, block_table, seq_lens, scale=None):
     """fp32 torch restatement of reference.py:20-49 on the GPU (large cases only)."""
     B, Hq, D = q.shape

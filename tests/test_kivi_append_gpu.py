@@ -114,3 +114,59 @@ def test_append_matches_golden_codes():
                         torch.from_numpy(c["block_table"]).cuda())
         gold = {k: v for k, v in golden_arrays().items() if k.startswith(spec["name"] + "/")}
         _compare(gc, {k.split("/", 1)[1]: v for k, v in gold.items()})
+
+
+@pytest.mark.parametrize("fmt", FORMATS)
+def test_append_error_bound_at_full_size(fmt):
+    """Size-independent properties of the GPU quantizer at the BASELINE KIVI size (B=8 x 32k
+    tokens, bs=64, 8 kv heads, D=128; N(0,1) keys with x10 outlier channels): every valid
+    dequantized value is within the rounding bound of the KIVI formula.
+    INT8 / INT4: |x - x_hat| <= s/2 + (Q s + |z|) 2^-10, where s and z are rounded to fp16.
+    FP8: |x - x_hat| <= |x| 2^-4 + s 2^-2 (e4m3 round-half-even, clamp at 448 s).
+    Codes stay inside the format's range."""
+    from bpt.quant import empty_kivi_cache, quantize_append
+    from test_kivi_decode_gpu import torch_dequant
+    B, ctx, bs, H, D = 8, 32768, 64, 8, 128
+    g = torch.Generator(device="cuda").manual_seed(11)
+    k = torch.randn(B, ctx, H, D, device="cuda", generator=g, dtype=torch.float16)
+    k[:, :, :, :4] *= 10   # outlier channels
+    v = torch.randn(B, ctx, H, D, device="cuda", generator=g, dtype=torch.float16)
+    lens = torch.randint(ctx // 2, ctx + 1, (B,), device="cuda", generator=g).to(torch.int32)
+    pages = ctx // bs
+    bt = torch.randperm(B * pages, device="cuda").reshape(B, pages).to(torch.int32)
+    cache = empty_kivi_cache(B * pages, bs, H, D, fmt)
+    quantize_append(cache, k, v, lens, torch.zeros_like(lens), bt)
+    torch.cuda.synchronize()
+    kd, vd = torch_dequant(cache, fmt)                   # [nb, bs, H, D] fp32
+    # originals in page layout, and which slots hold a valid token
+    kp = torch.zeros_like(kd)
+    vp = torch.zeros_like(vd)
+    valid = torch.zeros(B * pages, bs, dtype=torch.bool, device="cuda")
+    tok = torch.arange(ctx, device="cuda")
+    for b in range(B):
+        kp[bt[b]] = k[b].float().view(pages, bs, H, D)
+        vp[bt[b]] = v[b].float().view(pages, bs, H, D)
+        valid[bt[b]] = (tok < lens[b]).view(pages, bs)
+    m = valid[:, :, None, None]
+    ks = cache.k_scale.float()[:, None, :, :]            # per page, head, channel
+    vs = cache.v_scale.float()[:, :, :, None]            # per token, head
+    if fmt == "fp8":
+        kb = kp.abs() * 2.0 ** -4 + ks * 0.25
+        vb = vp.abs() * 2.0 ** -4 + vs * 0.25
+    else:
+        Q = 255.0 if fmt == "int8" else 15.0
+        kz = cache.k_zero.float()[:, None, :, :]
+        vz = cache.v_zero.float()[:, :, :, None]
+        kb = ks * 0.5 + (Q * ks + kz.abs()) * 2.0 ** -10 + 1e-6
+        vb = vs * 0.5 + (Q * vs + vz.abs()) * 2.0 ** -10 + 1e-6
+        top = int(Q)
+        codes_k = cache.k_codes if fmt == "int8" else torch.stack(
+            [cache.k_codes & 15, cache.k_codes >> 4], -1)
+        codes_v = cache.v_codes if fmt == "int8" else torch.stack(
+            [cache.v_codes & 15, cache.v_codes >> 4], -1)
+        assert int(codes_k.max()) <= top and int(codes_v.max()) <= top
+    assert bool((cache.k_scale.float() >= 0).all()) and bool((cache.v_scale.float() >= 0).all())
+    ek = ((kd - kp).abs() - kb).masked_fill(~m, -1.0)
+    ev = ((vd - vp).abs() - vb).masked_fill(~m, -1.0)
+    assert float(ek.max()) <= 0.0, f"{fmt} keys exceed the bound by {float(ek.max()):.3e}"
+    assert float(ev.max()) <= 0.0, f"{fmt} values exceed the bound by {float(ev.max()):.3e}"

@@ -118,14 +118,16 @@ def torch_dequant(cache, fmt):
     return kf, vf
 
 
-@pytest.mark.parametrize("fmt", ["int8", "fp8", "int4"])
-def test_full_size_quantized_batch(fmt):
-    """B=8 x ctx 32k (KIVI configuration), quantized on the GPU by the append kernel,
-    decoded, and checked against torch fp32 attention on the dequantized cache."""
+@pytest.mark.parametrize("fmt,B", [("int8", 8), ("fp8", 8), ("int4", 8), ("int8", 32),
+                                   ("fp8", 32), ("int4", 64)])
+def test_full_size_quantized_batch(fmt, B):
+    """B x ctx 32k at the BASELINE KIVI configurations (INT8 / FP8 B=32, INT4 B=64, and B=8),
+    quantized on the GPU by the append kernel, decoded, and checked against torch fp32
+    attention on the dequantized cache."""
     from bpt.cache import ragged_lengths
     from bpt.quant import empty_kivi_cache, paged_decode_attention_kivi, quantize_append
     from test_decode_gpu import torch_reference
-    B, ctx, bs, Hq, Hkv, D = 8, 32768, 64, 32, 8, 128
+    ctx, bs, Hq, Hkv, D = 32768, 64, 32, 8, 128
     lens = ragged_lengths(B, ctx, seed=3)
     g = torch.Generator(device="cuda").manual_seed(5)
     k = torch.randn(B, ctx, Hkv, D, device="cuda", generator=g, dtype=torch.float16)
@@ -141,4 +143,4 @@ def test_full_size_quantized_batch(fmt):
     del k, v
     for ns in (None, 1):
         out = paged_decode_attention_kivi(q, cache, bt, sl, num_splits=ns)
-        assert_close(out.float().cpu().numpy(), ref.cpu().numpy(), what=f"{fmt} B=8 ctx=32k")
+        assert_close(out.float().cpu().numpy(), ref.cpu().numpy(), what=f"{fmt} B={B} ctx=32k")
