@@ -67,10 +67,13 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", choices=["bpt", "reference", "reference-triton"], default="bpt",
+    ap.add_argument("--impl", choices=["bpt", "reference", "reference-triton", "flashinfer"],
+                    default="bpt",
                     help="reference: the reference's CPU algorithm (numpy port) on the host "
                          "cores; reference-triton: the reference's own Triton FP16 kernel "
-                         "(installed under baseline/_ref) on this GPU, same inputs")
+                         "(installed under baseline/_ref) on this GPU, same inputs; flashinfer: "
+                         "FlashInfer's paged decode (the library in this image) on this GPU, "
+                         "same inputs")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--no-e2e", action="store_true")
@@ -700,12 +703,97 @@ def run_reference_triton(args):
     return 0
 
 
+def run_flashinfer(args):
+    """--impl flashinfer: FlashInfer's BatchDecodeWithPagedKVCacheWrapper (NHD, planned once)
+    over the same seeded workload, timed per call with CUDA events over CUDA-graph replays
+    like the bpt arm. A comparison point (the decode kernel a serving stack would otherwise
+    call), not part of bpt. FP16, single GPU."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    wl = WORKLOADS[args.workload]
+    base = {"impl": "flashinfer", "metric": metric_name(wl),
+            "config": config_dict(args.workload, wl, 1)}
+    if wl["fmt"] != "fp16":
+        print(json.dumps({**base, "unavailable": "FlashInfer has no KIVI format"}))
+        return 0
+    import torch
+    try:
+        import flashinfer
+    except Exception as e:  # noqa: BLE001
+        print(json.dumps({**base, "unavailable": f"flashinfer import failed: {e}"}))
+        return 0
+    from bpt import decode as dec
+    from bpt.cache import random_paged_workload
+    from bpt.roofline import decode_call_bytes
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    bs = wl["block_size"]
+    lens = workload_lens(wl, 0, args.seed)
+    w = random_paged_workload(lens, HQ, HKV, D, bs, dev, seed=args.seed, spare_blocks=64)
+    q, kc, vc, bt, sl = w["q"], w["k_cache"], w["v_cache"], w["block_table"], w["seq_lens"]
+    pages = [(n + bs - 1) // bs for n in lens]
+    indices = torch.cat([bt[b, :p] for b, p in enumerate(pages)]).to(torch.int32)
+    indptr = torch.tensor([0] + list(torch.tensor(pages).cumsum(0)), dtype=torch.int32,
+                          device=dev)
+    last = torch.tensor([(n - 1) % bs + 1 for n in lens], dtype=torch.int32, device=dev)
+    fi = flashinfer.BatchDecodeWithPagedKVCacheWrapper(
+        torch.empty(256 << 20, dtype=torch.uint8, device=dev), "NHD")
+    fi.plan(indptr, indices, last, HQ, HKV, D, bs, q_data_type=torch.float16,
+            kv_data_type=torch.float16)
+    out = torch.empty_like(q)
+    call = lambda: fi.run(q, (kc, vc), out=out)  # noqa: E731
+    call()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        call()
+    stream.wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    timing = "CUDA-graph replay of one call per step"
+    try:
+        with torch.cuda.graph(graph):
+            call()
+        step = graph.replay
+    except Exception:  # noqa: BLE001
+        graph, step, timing = None, call, "eager calls"
+    for _ in range(max(args.warmup, 1)):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    nbytes = decode_call_bytes(lens, bs, HQ, HKV, D, "fp16")
+    mine = dec.paged_decode_attention(q, kc, vc, bt, sl)
+    torch.cuda.synchronize()
+    peak, peak_src = measured_peaks()
+    tbps = nbytes / (ms * 1e-3) / 1e12
+    print(json.dumps({**base, "value": tbps, "unit": "TB/s", "n_gpus": 1, "steps": args.steps,
+                      "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                      "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+                      "data": "synthetic (same seeded inputs as bpt)", "timing": timing,
+                      "flashinfer_version": getattr(flashinfer, "__version__", "?"),
+                      "frac_of_measured_hbm": tbps * 1e3 / peak, "peak_source": peak_src,
+                      "max_abs_diff_vs_bpt": (out.float() - mine.float()).abs().max().item()}),
+          flush=True)
+    del graph
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
     if args.impl == "reference-triton":
         return run_reference_triton(args)
+    if args.impl == "flashinfer":
+        return run_flashinfer(args)
     return run_bpt(args)
 
 
