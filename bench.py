@@ -19,7 +19,6 @@ algorithm (the numpy port in oracle/) on the host cores on a bounded sample of t
 """
 import argparse
 import json
-import math
 import os
 import statistics
 import sys

@@ -25,13 +25,12 @@ One process per GPU, ``torch.distributed`` with the NCCL backend over NVLink / N
   theirs and writes the merged output: two launches per call, capturable in a CUDA graph.
 """
 import ctypes
-from typing import List, Optional, Sequence, Tuple
+from typing import List, Optional, Tuple
 
 import torch
 import torch.distributed as dist
 
 from . import _lib
-from ._lib import BptArgumentError
 from .decode import _require, _stream_handle, merge_states_into, paged_decode_attention, \
     paged_decode_attention_partial
 

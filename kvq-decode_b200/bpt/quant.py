@@ -22,7 +22,6 @@ from typing import Optional
 import torch
 
 from . import _lib
-from ._lib import BptArgumentError
 from .decode import _require, _sm_count, _stream_handle, check_device_flags, CHECKS
 
 FORMATS = {"int8": 1, "fp8": 2, "int4": 3}

@@ -33,7 +33,7 @@ Storage (block_size = bs, kv heads = H, head dim = D, num_blocks = nb):
     k_scale, k_zero [nb, H, D] fp16;  v_scale, v_zero [nb, bs, H] fp16 (FP8: no zeros)
 Slots past a sequence's length inside its last page get code 0, v_scale 0, v_zero 0.
 """
-from typing import Optional, Sequence
+from typing import Sequence
 
 import numpy as np
 
