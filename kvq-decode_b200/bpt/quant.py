@@ -282,6 +282,46 @@ def paged_decode_attention_kivi_partial(q: torch.Tensor, cache: KiviCache,
     return o_part, lse
 
 
+def paged_decode_attention_kivi_with_residual(q: torch.Tensor, cache: KiviCache,
+                                             block_table: torch.Tensor, seq_lens: torch.Tensor,
+                                             k_res: torch.Tensor, v_res: torch.Tensor,
+                                             res_lens: torch.Tensor,
+                                             scale: Optional[float] = None,
+                                             num_splits: Optional[int] = None, *,
+                                             out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Decode over a KIVI cache whose newest tokens are still in full precision.
+
+    The append quantizer writes whole pages, because key statistics are per page. A decode
+    loop therefore keeps each sequence's not-yet-full last page in fp16 (KIVI's residual):
+    k_res / v_res [B, R, Hkv, D] fp16 hold sequence b's res_lens[b] newest tokens (positions
+    seq_lens[b] .. seq_lens[b] + res_lens[b] - 1; R a power of two >= 16, e.g. the page size).
+    When a residual fills a page, the caller moves it into the cache with ``quantize_append``
+    (start_pos = seq_lens[b], page-aligned) and empties it.
+
+    The quantized pages and the residual are decoded by their own kernels into per-split
+    partial softmax states. Those are merged in one pass (the split merge), so the result is
+    attention over the union: the quantized part as fp32 math on the dequantized cache, the
+    residual in fp16 as ``paged_decode_attention``.
+    """
+    from .decode import merge_partials, paged_decode_attention_partial
+    B, Hq, D = _validate_decode(q, cache, block_table, seq_lens)
+    _require(k_res.dim() == 4 and k_res.shape == v_res.shape and k_res.shape[0] == B and
+             tuple(k_res.shape[2:]) == (cache.kv_heads, D) and
+             k_res.dtype == v_res.dtype == torch.float16,
+             "k_res / v_res must be float16 [B, R, Hkv, D] matching q and the cache")
+    _require(res_lens.shape == (B,) and res_lens.dtype == torch.int32 and
+             res_lens.device == q.device, "res_lens must be int32 [B] on q's device")
+    R = k_res.shape[1]
+    # the residual as a paged fp16 cache: one page of R tokens per sequence
+    bt_res = torch.arange(B, dtype=torch.int32, device=q.device).view(B, 1)
+    o_q, l_q = paged_decode_attention_kivi_partial(q, cache, block_table, seq_lens, scale,
+                                                   num_splits)
+    o_r, l_r = paged_decode_attention_partial(q, k_res, v_res, bt_res, res_lens, scale,
+                                              max(1, min(4, R // 16)))
+    return merge_partials(torch.cat([o_q, o_r], dim=2).contiguous(),
+                          torch.cat([l_q, l_r], dim=2).contiguous(), out=out)
+
+
 def random_kivi_workload(lens, q_heads: int, kv_heads: int, head_dim: int, block_size: int,
                          fmt: str, device, seed: int = 0, outlier_channels: int = 4,
                          outlier_scale: float = 10.0, spare_blocks: int = 0,
@@ -331,5 +371,6 @@ def random_kivi_workload(lens, q_heads: int, kv_heads: int, head_dim: int, block
 
 __all__ = ["KiviCache", "KiviCacheC", "empty_kivi_cache", "quantize_append", "FORMATS",
            "paged_decode_attention_kivi", "paged_decode_attention_kivi_partial",
+           "paged_decode_attention_kivi_with_residual",
            "effective_splits_kivi",
            "random_kivi_workload"]

@@ -144,3 +144,46 @@ def test_full_size_quantized_batch(fmt, B):
     for ns in (None, 1):
         out = paged_decode_attention_kivi(q, cache, bt, sl, num_splits=ns)
         assert_close(out.float().cpu().numpy(), ref.cpu().numpy(), what=f"{fmt} B={B} ctx=32k")
+
+
+@pytest.mark.parametrize("fmt", ["int8", "fp8", "int4"])
+def test_decode_with_fp16_residual(fmt):
+    """A decode loop's view of a KIVI cache: full pages quantized, the newest tokens (a
+    partial page, 0..63 of them) still fp16. paged_decode_attention_kivi_with_residual must
+    equal fp32 attention over [dequantized pages ; fp16 residual] (numpy, per sequence)."""
+    from bpt.quant import paged_decode_attention_kivi_with_residual
+    from oracle.cache import block_table_for, make_qkv, rng
+    bs, Hq, Hkv, D, R = 64, 32, 8, 128, 64
+    total = [300, 64, 5, 1000, 127]
+    nq = [(n // bs) * bs for n in total]            # quantized, page-aligned
+    nr = [n - m for n, m in zip(total, nq)]         # residual, < one page
+    g = rng(21)
+    q, k, v = make_qkv(g, total, Hq, Hkv, D, outlier_channels=4)
+    bt, nb = block_table_for(g, [max(m, 1) for m in nq], bs, "spare", 4)
+    cache = kivi.empty_cache(nb, bs, Hkv, D, fmt)
+    kivi.quantize_append(cache, k, v, nq, [0] * len(total), bt, bs, fmt)
+    kd, vd = kivi.dequantize_cache(cache, fmt)
+    k_res = np.zeros((len(total), R, Hkv, D), np.float16)
+    v_res = np.zeros_like(k_res)
+    for b, (m, r) in enumerate(zip(nq, nr)):
+        k_res[b, :r] = k[b, m:m + r]
+        v_res[b, :r] = v[b, m:m + r]
+    # reference: fp32 attention over the dequantized pages followed by the fp16 residual
+    ref = np.zeros((len(total), Hq, D), np.float32)
+    group = Hq // Hkv
+    for b, (m, r) in enumerate(zip(nq, nr)):
+        pages = bt[b, :(m + bs - 1) // bs]
+        kk = np.concatenate([kd[pages].reshape(-1, Hkv, D)[:m], k_res[b, :r].astype(np.float32)])
+        vv = np.concatenate([vd[pages].reshape(-1, Hkv, D)[:m], v_res[b, :r].astype(np.float32)])
+        for hq in range(Hq):
+            s = kk[:, hq // group] @ q[b, hq].astype(np.float32) / np.sqrt(D)
+            p = np.exp(s - s.max())
+            ref[b, hq] = (p / p.sum()) @ vv[:, hq // group]
+    gc = to_gpu_cache(cache, fmt, bs)
+    args = (torch.from_numpy(q).cuda(), gc, torch.from_numpy(bt).cuda(),
+            torch.tensor(nq, dtype=torch.int32, device="cuda"),
+            torch.from_numpy(k_res).cuda(), torch.from_numpy(v_res).cuda(),
+            torch.tensor(nr, dtype=torch.int32, device="cuda"))
+    for ns in (None, 1):
+        out = paged_decode_attention_kivi_with_residual(*args, num_splits=ns)
+        assert_close(out.float().cpu().numpy(), ref, what=f"{fmt} residual ns={ns}")
