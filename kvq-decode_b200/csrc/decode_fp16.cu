@@ -408,104 +408,123 @@ struct MergeLayout {
   int64_t l_ss, l_sb, l_sh;   // partial lse strides
 };
 
-template <bool F16OUT>
-__global__ void __launch_bounds__(128)
+constexpr int kMergeWarps = 8;   // most warps per merge CTA
+constexpr int kMergeRows = 16;   // partial rows a warp loads before using any
+
+// 4 consecutive channels 4c .. 4c + 3 of one partial row (zero past D)
+template <bool VEC>
+__device__ __forceinline__ float4 load_row4(const float* row, int c, int D) {
+  if constexpr (VEC) return __ldg(reinterpret_cast<const float4*>(row) + c);
+  const int d = 4 * c;
+  return make_float4(row[d], d + 1 < D ? row[d + 1] : 0.f, d + 2 < D ? row[d + 2] : 0.f,
+                     d + 3 < D ? row[d + 3] : 0.f);
+}
+
+template <bool F16OUT, bool VEC>
+__global__ void __launch_bounds__(kMergeWarps * 32)
 merge_splits_kernel(const float* __restrict__ o_part, const float* __restrict__ lse,
                     const MergeLayout lay, int q_heads, int splits, int D,
                     __half* __restrict__ out16, int64_t o_sb, int64_t o_sh,
                     float* __restrict__ o32, float* __restrict__ lse32) {
-  // One CTA per (q head, sequence). The S partial rows are spread over the 4 warps (warp w
-  // takes splits w, w + 4, ...) and each lane holds 4 consecutive channels, so a warp keeps
-  // several independent 16-byte loads in flight instead of walking the splits one dependent
-  // load at a time; the 4 warp sums are added through shared memory.
-  extern __shared__ float w_s[];  // [splits]
-  __shared__ float red[4];
-  __shared__ float4 part[4][64];  // per-warp sums, D <= 256
+  // One CTA per (q head, sequence) of W = ceil(S / 16) <= 8 warps. Warp w owns splits w,
+  // w + W, w + 2W, ... and merges them online in batches of kMergeRows rows: every load of a
+  // batch (each row's lse and this lane's 4 channels of its o row) is issued before any is
+  // used, so up to 128 partial rows cost one memory round trip. Lane l holds channels
+  // 4 (32 g + l) .. + 3 of channel group g (one group for D <= 128). The W warp states
+  // (max, sum, o) are then combined through shared memory in warp order, so the result does
+  // not depend on timing. VEC: o rows are 16-byte aligned with D % 4 == 0 (float4 loads).
+  constexpr int R = kMergeRows;
+  const int W = int(blockDim.x) >> 5;
+  __shared__ float s_m[kMergeWarps], s_l[kMergeWarps];
+  __shared__ float4 s_o[kMergeWarps][32];
   const int hq = blockIdx.x, b = blockIdx.y;
   const float* l = lse + int64_t(b) * lay.l_sb + int64_t(hq) * lay.l_sh;
   const float* o = o_part + int64_t(b) * lay.o_sb + int64_t(hq) * lay.o_sh;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nd4 = (D + 3) >> 2;
   pdl_wait();
 
-  float m = kNegInf;
-  for (int s = tid; s < splits; s += blockDim.x) m = fmaxf(m, l[s * lay.l_ss]);
+  for (int c0 = 0; c0 < nd4; c0 += 32) {
+    const int c = c0 + lane;
+    const bool c_in = c < nd4;
+    float m = kNegInf, wsum = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s0 = warp; s0 < splits; s0 += W * R) {
+      float ls[R];
+      float4 v[R];
 #pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(kFullMask, m, off));
-  if (lane == 0) red[warp] = m;
-  __syncthreads();
-  const float M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-  __syncthreads();
-  float wsum = 0.f;
-  for (int s = tid; s < splits; s += blockDim.x) {
-    const float w = (M == kNegInf) ? 0.f : fast_exp2(l[s * lay.l_ss] - M);
-    w_s[s] = w;
-    wsum += w;
-  }
-#pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) wsum += __shfl_xor_sync(kFullMask, wsum, off);
-  if (lane == 0) red[warp] = wsum;
-  __syncthreads();
-  const float W = red[0] + red[1] + red[2] + red[3];
-  const float invW = W > 0.f ? 1.f / W : 0.f;
-  auto put = [&](int d, float a) {
-    const float r = W > 0.f ? a * invW : 0.f;
-    if constexpr (F16OUT) {
-      out16[int64_t(b) * o_sb + int64_t(hq) * o_sh + d] = __float2half_rn(r);
-    } else {
-      o32[(int64_t(b) * q_heads + hq) * D + d] = r;
-    }
-  };
-  // a split of weight 0 contributes nothing even if its row holds garbage (select, not branch,
-  // so the loads stay independent)
-  const bool vec = (D % 4 == 0) && D <= 256 && (lay.o_ss % 4 == 0) &&
-                   ((reinterpret_cast<uintptr_t>(o) & 15) == 0);
-  if (vec) {
-    const int nd4 = D >> 2;
-    for (int c = lane; c < nd4; c += 32) {
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      auto add = [&](int s) {
-        const float4 v = __ldg(reinterpret_cast<const float4*>(o + s * lay.o_ss) + c);
-        const float w = w_s[s];
-        const bool on = w != 0.f;
-        acc.x = fmaf(w, on ? v.x : 0.f, acc.x);
-        acc.y = fmaf(w, on ? v.y : 0.f, acc.y);
-        acc.z = fmaf(w, on ? v.z : 0.f, acc.z);
-        acc.w = fmaf(w, on ? v.w : 0.f, acc.w);
-      };
-      int s = warp;
-      for (; s + 28 < splits; s += 32) {
-#pragma unroll
-        for (int u = 0; u < 32; u += 4) add(s + u);
+      for (int u = 0; u < R; ++u) {
+        const int s = s0 + W * u;
+        const bool in = s < splits;
+        ls[u] = in ? l[int64_t(s) * lay.l_ss] : kNegInf;
+        v[u] = (in && c_in) ? load_row4<VEC>(o + int64_t(s) * lay.o_ss, c, D)
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
       }
-      for (; s + 12 < splits; s += 16) {
+      float mb = m;
 #pragma unroll
-        for (int u = 0; u < 16; u += 4) add(s + u);
+      for (int u = 0; u < R; ++u) mb = fmaxf(mb, ls[u]);
+      if (mb != kNegInf) {   // warp-uniform: every lane holds the same lse values
+        const float f = fast_exp2(m - mb);   // 0 while m is -inf
+        wsum *= f;
+        acc.x *= f; acc.y *= f; acc.z *= f; acc.w *= f;
+#pragma unroll
+        for (int u = 0; u < R; ++u) {
+          // a split of weight 0 contributes nothing even if its row holds garbage (select,
+          // not branch, so the loads stay independent)
+          const float w = fast_exp2(ls[u] - mb);
+          const bool on = w != 0.f;
+          wsum += w;
+          acc.x = fmaf(w, on ? v[u].x : 0.f, acc.x);
+          acc.y = fmaf(w, on ? v[u].y : 0.f, acc.y);
+          acc.z = fmaf(w, on ? v[u].z : 0.f, acc.z);
+          acc.w = fmaf(w, on ? v[u].w : 0.f, acc.w);
+        }
+        m = mb;
       }
-      for (; s < splits; s += 4) add(s);
-      part[warp][c] = acc;
     }
+    if (lane == 0) {
+      s_m[warp] = m;
+      s_l[warp] = wsum;
+    }
+    s_o[warp][lane] = acc;
     __syncthreads();
-    for (int c = tid; c < nd4; c += blockDim.x) {
-      const float4 a0 = part[0][c], a1 = part[1][c], a2 = part[2][c], a3 = part[3][c];
-      put(4 * c + 0, (a0.x + a1.x) + (a2.x + a3.x));
-      put(4 * c + 1, (a0.y + a1.y) + (a2.y + a3.y));
-      put(4 * c + 2, (a0.z + a1.z) + (a2.z + a3.z));
-      put(4 * c + 3, (a0.w + a1.w) + (a2.w + a3.w));
-    }
-  } else {
-    for (int d = tid; d < D; d += blockDim.x) {
-      float a = 0.f;
-#pragma unroll 8
-      for (int s = 0; s < splits; ++s) {
-        const float w = w_s[s];
-        const float v = o[s * lay.o_ss + d];
-        a = fmaf(w, w != 0.f ? v : 0.f, a);
+    if (warp == 0) {
+      float M = kNegInf;
+      for (int w = 0; w < W; ++w) M = fmaxf(M, s_m[w]);
+      float L = 0.f;
+      float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (M != kNegInf) {
+        for (int w = 0; w < W; ++w) {
+          const float f = fast_exp2(s_m[w] - M);
+          const float4 a = s_o[w][lane];
+          L = fmaf(s_l[w], f, L);
+          O.x = fmaf(a.x, f, O.x);
+          O.y = fmaf(a.y, f, O.y);
+          O.z = fmaf(a.z, f, O.z);
+          O.w = fmaf(a.w, f, O.w);
+        }
       }
-      put(d, a);
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+      const float r[4] = {O.x * inv, O.y * inv, O.z * inv, O.w * inv};
+      if (c_in) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int d = 4 * c + e;
+          if (d < D) {
+            if constexpr (F16OUT) {
+              out16[int64_t(b) * o_sb + int64_t(hq) * o_sh + d] = __float2half_rn(r[e]);
+            } else {
+              o32[(int64_t(b) * q_heads + hq) * D + d] = r[e];
+            }
+          }
+        }
+      }
+      if constexpr (!F16OUT) {
+        if (c0 == 0 && lane == 0)
+          lse32[int64_t(b) * q_heads + hq] = L > 0.f ? M + __log2f(L) : kNegInf;
+      }
     }
-  }
-  if constexpr (!F16OUT) {
-    if (tid == 0) lse32[int64_t(b) * q_heads + hq] = W > 0.f ? M + __log2f(W) : kNegInf;
+    __syncthreads();   // s_m / s_l / s_o are rewritten by the next channel group
   }
 }
 
@@ -581,26 +600,34 @@ static int launch_merge_layout(const float* o_part, const float* lse, const Merg
                                int64_t o_sb, int64_t o_sh, float* o32, float* lse32,
                                cudaStream_t st, bool pdl) {
   if (batch <= 0) return BPT_OK;
-  const size_t sm = size_t(splits) * sizeof(float);
-  if (sm > 48 * 1024) return BPT_ERR_UNSUPPORTED_SHAPE;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(q_heads, batch);
-  cfg.blockDim = dim3(128);
-  cfg.dynamicSmemBytes = sm;
+  const int warps = splits >= kMergeWarps * kMergeRows ? kMergeWarps
+                                                        : (splits + kMergeRows - 1) / kMergeRows;
+  cfg.blockDim = dim3(32 * (warps < 1 ? 1 : warps));
+  cfg.dynamicSmemBytes = 0;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
+  // float4 loads when every (b, head, split) row starts on a 16-byte boundary
+  const bool vec = (D % 4 == 0) && (lay.o_ss % 4 == 0) && (lay.o_sb % 4 == 0) &&
+                   (lay.o_sh % 4 == 0) && ((reinterpret_cast<uintptr_t>(o_part) & 15) == 0);
+  float* const no32 = nullptr;
+  __half* const no16 = nullptr;
   cudaError_t e;
   if (out16) {
-    e = cudaLaunchKernelEx(&cfg, merge_splits_kernel<true>, o_part, lse, lay, q_heads, splits,
-                           D, out16, o_sb, o_sh, static_cast<float*>(nullptr),
-                           static_cast<float*>(nullptr));
+    e = vec ? cudaLaunchKernelEx(&cfg, merge_splits_kernel<true, true>, o_part, lse, lay,
+                                 q_heads, splits, D, out16, o_sb, o_sh, no32, no32)
+            : cudaLaunchKernelEx(&cfg, merge_splits_kernel<true, false>, o_part, lse, lay,
+                                 q_heads, splits, D, out16, o_sb, o_sh, no32, no32);
   } else {
-    e = cudaLaunchKernelEx(&cfg, merge_splits_kernel<false>, o_part, lse, lay, q_heads, splits,
-                           D, static_cast<__half*>(nullptr), int64_t(0), int64_t(0), o32, lse32);
+    e = vec ? cudaLaunchKernelEx(&cfg, merge_splits_kernel<false, true>, o_part, lse, lay,
+                                 q_heads, splits, D, no16, int64_t(0), int64_t(0), o32, lse32)
+            : cudaLaunchKernelEx(&cfg, merge_splits_kernel<false, false>, o_part, lse, lay,
+                                 q_heads, splits, D, no16, int64_t(0), int64_t(0), o32, lse32);
   }
   return e == cudaSuccess ? BPT_OK : BPT_ERR_LAUNCH;
 }
