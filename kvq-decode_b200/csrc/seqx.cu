@@ -22,12 +22,12 @@
 // set is never overwritten while a peer may still read it.
 //
 // Per call, every CTA takes items (b, hq) = blockIdx.x, blockIdx.x + gridDim.x, ...:
-//   phase 1: merge this rank's S split rows of the item into one state (o, lse2) and store it,
-//            epoch-tagged, into slot (rank, item) of every rank's buffer (peer stores over
-//            NVLink);
-//   phase 2: each thread polls (time-bounded) the words it needs in the local buffer until they
-//            carry the epoch -- one lse2 per rank, then its channels of every rank's o -- and the
-//            CTA merges the world states into the fp16 output.
+//   phase 1: merge this rank's S split rows of the item into one state (o, lse2), reading up
+//            to 128 split rows in one memory round trip, and store it, epoch-tagged, into slot
+//            (rank, item) of every rank's buffer (peer stores over NVLink);
+//   phase 2: thread d reads the words it needs in the local buffer -- every rank's lse2 and
+//            o[d] -- all at once, polls (time-bounded) those that do not carry the epoch yet,
+//            and merges the world states into channel d of the fp16 output.
 // A CTA finishes all its phase-1 stores before it waits, and the grid never exceeds what is
 // resident at once, so no rank can wait on a CTA that cannot start. The epoch is
 // ctl[0] + 1; the last CTA to finish bumps ctl[0], so consecutive calls (also graph replays)
@@ -46,7 +46,9 @@ namespace bpt {
 namespace {
 
 constexpr int kMaxRanks = 8;
-constexpr int kThreads = 128;
+constexpr int kWarps = 8;
+constexpr int kThreads = 32 * kWarps;
+constexpr int kRows = 16;   // split rows a warp loads before using any
 constexpr float kNegInf = -INFINITY;
 
 struct RankBufs {
@@ -69,11 +71,11 @@ __device__ __forceinline__ uint64_t ld_tagged(const uint64_t* p) {
   return w;
 }
 
-// Wait (time-bounded) until word p carries `epoch`; returns its value (0 after a timeout; once
-// a thread timed out it stops waiting for later words).
-__device__ __forceinline__ float wait_tagged(const uint64_t* p, unsigned epoch, uint64_t budget_ns,
-                                             int* timed_out) {
-  uint64_t w = ld_tagged(p);
+// The value of word p for this call, given a first read w of it: if w does not carry `epoch`
+// yet, poll (time-bounded) until it does. Returns 0 after a timeout; once a thread timed out it
+// stops waiting for later words.
+__device__ __forceinline__ float finish_tagged(const uint64_t* p, uint64_t w, unsigned epoch,
+                                               uint64_t budget_ns, int* timed_out) {
   if (unsigned(w >> 32) != epoch) {
     if (*timed_out) return 0.f;
     const uint64_t t0 = global_timer_ns();
@@ -93,10 +95,8 @@ seq_exchange_kernel(const float* __restrict__ o_part, const float* __restrict__ 
                     int q_heads, int splits, int D, RankBufs bufs, int world, int rank,
                     __half* __restrict__ out, int64_t o_sb, int64_t o_sh, unsigned* status,
                     uint64_t budget_ns) {
-  extern __shared__ float w_s[];      // [splits]
-  __shared__ float red[4];
-  __shared__ float4 part[4][64];      // per-warp sums, D <= 256
-  __shared__ float st_lse[kMaxRanks];
+  __shared__ float s_m[kWarps], s_l[kWarps];
+  __shared__ float4 s_o[kWarps][32];
   __shared__ int timed_out;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int items = batch * q_heads;
@@ -111,88 +111,129 @@ seq_exchange_kernel(const float* __restrict__ o_part, const float* __restrict__ 
   int my_timeout = 0;
   if (tid == 0) timed_out = 0;
 
-  // ---- phase 1: local split merge, epoch-tagged stores into every rank's slot (rank, item)
+  // ---- phase 1: local split merge, epoch-tagged stores into every rank's slot (rank, item).
+  // Warp w owns splits w, w + 8, ... and merges them online in batches of kRows rows, every
+  // load of a batch (the rows' lse and this lane's 4 channels of their o) issued before any is
+  // used; the 8 warp states are combined in warp order through shared memory.
   for (int it = blockIdx.x; it < items; it += gridDim.x) {
     const float* l = lse + int64_t(it) * splits;
     const float* o = o_part + int64_t(it) * splits * D;
-    float m = kNegInf;
-    for (int s = tid; s < splits; s += kThreads) m = fmaxf(m, l[s]);
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(kFullMask, m, off));
-    if (lane == 0) red[warp] = m;
-    __syncthreads();
-    const float M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-    __syncthreads();
-    float wsum = 0.f;
-    for (int s = tid; s < splits; s += kThreads) {
-      const float w = (M == kNegInf) ? 0.f : fast_exp2(l[s] - M);
-      w_s[s] = w;
-      wsum += w;
-    }
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) wsum += __shfl_xor_sync(kFullMask, wsum, off);
-    if (lane == 0) red[warp] = wsum;
-    __syncthreads();
-    const float W = red[0] + red[1] + red[2] + red[3];
-    for (int c = lane; c < nd4; c += 32) {
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int s = warp; s < splits; s += 4) {
-        const float4 v = __ldg(reinterpret_cast<const float4*>(o + int64_t(s) * D) + c);
-        const float w = w_s[s];
-        const bool on = w != 0.f;
-        acc.x = fmaf(w, on ? v.x : 0.f, acc.x);
-        acc.y = fmaf(w, on ? v.y : 0.f, acc.y);
-        acc.z = fmaf(w, on ? v.z : 0.f, acc.z);
-        acc.w = fmaf(w, on ? v.w : 0.f, acc.w);
-      }
-      part[warp][c] = acc;
-    }
-    __syncthreads();
-    const float invW = W > 0.f ? 1.f / W : 0.f;
-    const float* pf = reinterpret_cast<const float*>(&part[0][0]);
     const size_t base = set0 + (size_t(rank) * items + it) * slot_words(D);
-    for (int d = tid; d < D; d += kThreads) {
-      // channel d of the 4 warp sums: part[w][d / 4].{x,y,z,w}[d % 4]
-      const float v = ((pf[d] + pf[256 + d]) + (pf[512 + d] + pf[768 + d])) * invW;
-      for (int r = 0; r < world; ++r) st_tagged(slots[r] + base + d, v, epoch);
+    for (int c0 = 0; c0 < nd4; c0 += 32) {
+      const int c = c0 + lane;
+      const bool c_in = c < nd4;
+      float m = kNegInf, wsum = 0.f;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int s0 = warp; s0 < splits; s0 += kWarps * kRows) {
+        float ls[kRows];
+        float4 v[kRows];
+#pragma unroll
+        for (int u = 0; u < kRows; ++u) {
+          const int sp = s0 + kWarps * u;
+          const bool in = sp < splits;
+          ls[u] = in ? l[sp] : kNegInf;
+          v[u] = (in && c_in) ? __ldg(reinterpret_cast<const float4*>(o + int64_t(sp) * D) + c)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        float mb = m;
+#pragma unroll
+        for (int u = 0; u < kRows; ++u) mb = fmaxf(mb, ls[u]);
+        if (mb != kNegInf) {   // warp-uniform
+          const float f = fast_exp2(m - mb);
+          wsum *= f;
+          acc.x *= f; acc.y *= f; acc.z *= f; acc.w *= f;
+#pragma unroll
+          for (int u = 0; u < kRows; ++u) {
+            // a split of weight 0 contributes nothing even if its row holds garbage
+            const float w = fast_exp2(ls[u] - mb);
+            const bool on = w != 0.f;
+            wsum += w;
+            acc.x = fmaf(w, on ? v[u].x : 0.f, acc.x);
+            acc.y = fmaf(w, on ? v[u].y : 0.f, acc.y);
+            acc.z = fmaf(w, on ? v[u].z : 0.f, acc.z);
+            acc.w = fmaf(w, on ? v[u].w : 0.f, acc.w);
+          }
+          m = mb;
+        }
+      }
+      if (lane == 0) {
+        s_m[warp] = m;
+        s_l[warp] = wsum;
+      }
+      s_o[warp][lane] = acc;
+      __syncthreads();
+      if (warp == 0) {
+        float M = kNegInf;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) M = fmaxf(M, s_m[w]);
+        float L = 0.f;
+        float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (M != kNegInf) {
+#pragma unroll
+          for (int w = 0; w < kWarps; ++w) {
+            const float f = fast_exp2(s_m[w] - M);
+            const float4 a4 = s_o[w][lane];
+            L = fmaf(s_l[w], f, L);
+            O.x = fmaf(a4.x, f, O.x);
+            O.y = fmaf(a4.y, f, O.y);
+            O.z = fmaf(a4.z, f, O.z);
+            O.w = fmaf(a4.w, f, O.w);
+          }
+        }
+        const float inv = L > 0.f ? 1.f / L : 0.f;
+        if (c_in) {
+          const float r4[4] = {O.x * inv, O.y * inv, O.z * inv, O.w * inv};
+          for (int r = 0; r < world; ++r)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) st_tagged(slots[r] + base + 4 * c + e, r4[e], epoch);
+        }
+        if (c0 == 0 && lane < world)
+          st_tagged(slots[lane] + base + D, L > 0.f ? M + __log2f(L) : kNegInf, epoch);
+      }
+      __syncthreads();   // s_m / s_l / s_o are rewritten next
     }
-    if (tid < world)
-      st_tagged(slots[tid] + base + D, W > 0.f ? M + __log2f(W) : kNegInf, epoch);
-    __syncthreads();   // part / w_s / red are reused by the next item
   }
 
-  // ---- phase 2: wait for every rank's state of my items, merge them
+  // ---- phase 2: every rank's state of my items -> the merged fp16 output. Thread d reads
+  // every rank's lse word and o word d at once, then polls (time-bounded) only the words that
+  // do not carry this call's epoch yet. Every word is awaited, even at weight 0, so no store
+  // of this call is still in flight into the buffer when the next call starts.
   for (int it = blockIdx.x; it < items; it += gridDim.x) {
-    if (tid < world)
-      st_lse[tid] = wait_tagged(mine + (size_t(tid) * items + it) * slot_words(D) + D, epoch,
-                                budget_ns, &my_timeout);
-    __syncthreads();
-    float M = kNegInf;
-    for (int r = 0; r < world; ++r) M = fmaxf(M, st_lse[r]);
-    float wr[kMaxRanks];
-    float W = 0.f;
-#pragma unroll
-    for (int r = 0; r < kMaxRanks; ++r) {
-      wr[r] = (r < world && M != kNegInf) ? fast_exp2(st_lse[r] - M) : 0.f;
-      W += wr[r];
-    }
-    const float invW = W > 0.f ? 1.f / W : 0.f;
     const int b = it / q_heads, hq = it % q_heads;
+    const uint64_t* item0 = mine + size_t(it) * slot_words(D);
+    const size_t rstride = size_t(items) * slot_words(D);
     for (int d = tid; d < D; d += kThreads) {
-      float acc = 0.f;
+      uint64_t lw[kMaxRanks], ow[kMaxRanks];
 #pragma unroll
       for (int r = 0; r < kMaxRanks; ++r) {
         if (r < world) {
-          // every rank's word is awaited (even at weight 0) so no store of this call is
-          // still in flight into the buffer when the next call starts
-          const float v = wait_tagged(mine + (size_t(r) * items + it) * slot_words(D) + d,
-                                      epoch, budget_ns, &my_timeout);
-          if (wr[r] != 0.f) acc = fmaf(wr[r], v, acc);
+          lw[r] = ld_tagged(item0 + r * rstride + D);
+          ow[r] = ld_tagged(item0 + r * rstride + d);
         }
       }
-      out[int64_t(b) * o_sb + int64_t(hq) * o_sh + d] = __float2half_rn(acc * invW);
+      float ls[kMaxRanks], ov[kMaxRanks];
+      float M = kNegInf;
+#pragma unroll
+      for (int r = 0; r < kMaxRanks; ++r) {
+        ls[r] = kNegInf;
+        ov[r] = 0.f;
+        if (r < world) {
+          ls[r] = finish_tagged(item0 + r * rstride + D, lw[r], epoch, budget_ns, &my_timeout);
+          ov[r] = finish_tagged(item0 + r * rstride + d, ow[r], epoch, budget_ns, &my_timeout);
+          M = fmaxf(M, ls[r]);
+        }
+      }
+      float W = 0.f, acc = 0.f;
+      if (M != kNegInf) {
+#pragma unroll
+        for (int r = 0; r < kMaxRanks; ++r) {
+          const float w = r < world ? fast_exp2(ls[r] - M) : 0.f;
+          W += w;
+          if (w != 0.f) acc = fmaf(w, ov[r], acc);
+        }
+      }
+      out[int64_t(b) * o_sb + int64_t(hq) * o_sh + d] = __float2half_rn(W > 0.f ? acc / W : 0.f);
     }
-    __syncthreads();   // st_lse is reused by the next item
   }
 
   // ---- the last CTA to finish publishes this call's epoch
@@ -215,7 +256,7 @@ int resident_grid() {
   if (cached) return cached;
   int per_sm = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, seq_exchange_kernel, kThreads,
-                                                    4096) != cudaSuccess ||
+                                                    0) != cudaSuccess ||
       per_sm < 1)
     per_sm = 1;
   cached = per_sm * device_sm_count();
@@ -289,15 +330,13 @@ extern "C" int bpt_seqx_merge_fp16(const float* o_part, const float* lse, int ba
     if (!bufs[r] || (reinterpret_cast<uintptr_t>(bufs[r]) & 15)) return BPT_ERR_INVALID_ARGUMENT;
     rb.p[r] = static_cast<float*>(bufs[r]);
   }
-  const size_t smem = size_t(splits) * sizeof(float);
-  if (smem > 48 * 1024) return BPT_ERR_UNSUPPORTED_SHAPE;
   const int items = batch * q_heads;
   int grid = resident_grid();
   if (grid > items) grid = items;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = smem;
+  cfg.dynamicSmemBytes = 0;
   cfg.stream = static_cast<cudaStream_t>(stream);
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
