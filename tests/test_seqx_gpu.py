@@ -45,10 +45,12 @@ def _merge(o, lse, bufs, rank, status, out, budget_us=2_000_000):
                                 budget_us, torch.cuda.current_stream().cuda_stream)
 
 
-def test_world1_equals_split_merge_and_replays():
+@pytest.mark.parametrize("S,D", [(9, 128), (200, 128), (74, 256), (130, 64)])
+def test_world1_equals_split_merge_and_replays(S, D):
+    """S > 128 takes more than one batch of split rows per warp; D = 256 two channel groups."""
     from bpt.decode import merge_partials
     from bpt.dist import _seqx_fns
-    o, lse = _partials()
+    o, lse = _partials(S=S, D=D)
     B, Hq, S, D = o.shape
     ref = merge_partials(o, lse)
     buf = _buffer(1, B, Hq, D)
