@@ -498,7 +498,8 @@ def run_bpt(args):
         torch.cuda.synchronize()
     barrier()
     elapsed_ms = t_start.elapsed_time(t_end)
-    kern_ms = sum(a.elapsed_time(b) for a, b in evs) / max(args.steps, 1)
+    call_ms = [a.elapsed_time(b) for a, b in evs]
+    kern_ms = sum(call_ms) / max(args.steps, 1)
 
     tot = torch.tensor([elapsed_ms, step_bytes * args.steps], dtype=torch.float64, device=dev)
     if world > 1:
@@ -618,7 +619,11 @@ def run_bpt(args):
                      "frac": achieved_gbs / peak, "peak_source": peak_src,
                      "traffic": traffic, "traffic_note": traffic_note,
                      "algorithmic_bytes_per_launch": kernel_bytes,
-                     "kernel_ms_per_launch": kern_ms},
+                     "kernel_ms_per_launch": kern_ms,
+                     # this rank's per-call CUDA-event times over the timed steps
+                     "call_us": {"mean": kern_ms * 1e3,
+                                 "median": statistics.median(call_ms) * 1e3 if call_ms else None,
+                                 "min": min(call_ms) * 1e3 if call_ms else None}},
         "cpu_baseline": cpu,
         "e2e": e2e,
         "gpu_launches": args.steps * launches_per_step,
