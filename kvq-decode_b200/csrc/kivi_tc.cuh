@@ -6,15 +6,24 @@
 //
 //   QK^T   D_qk[token][16 j + 4 h + limb] = sum_k K[token][k] * B_qk[16 j + 4 h + limb][k]
 //          M = 128 tokens, N = 16 per page slot j, K = 128 channel bytes (4 MMAs of 32).
-//          A = the key code tile exactly as TMA stored it (K-major, 128-byte swizzle; INT4
-//          codes are first split into a low-nibble and a high-nibble half row). B = the q'
-//          limbs: x = round(q * k_scale * 2^Ek) (|x| < 2^22) as three balanced signed bytes,
-//          written by the warps in the same K-major swizzled layout.
+//          A = the key code tile exactly as TMA stored it (K-major, 128-byte swizzle). B = the
+//          q' limbs: x = round(q * k_scale * 2^Ek) (|x| < 2^22) as three balanced signed
+//          bytes, written by the warps in the same K-major swizzled layout.
+//          INT4: a packed byte is lo + 16 hi (lo = even channel), so
+//            sum_k lo_k x_2k + hi_k x_2k+1 = sum_k byte_k v_k + lo_k (x_2k - v_k),
+//          v_k = round(x_2k+1 / 16) (the odd channels' x taken as 16 v_k; INT4 x uses four
+//          limbs, |x| < 2^26, so v keeps 22 bits). Two MMAs read the
+//          packed tile as TMA stored it (64-byte rows, 64-byte swizzle) against B rows of v,
+//          two read a low-nibble copy (one AND per word, same layout) against rows of x_2k - v.
 //          S_h = (L0 + 256 L1 + 65536 L2) * 2^-Ek + sum_d q_d k_zero_d            (fp32)
 //   P.V    D_pv[channel][4 h + limb] += sum_t V[t][channel] * P'[t][4 h + limb]
 //          M = 128 channels, N = 16, K = 128 tokens. A = the value code tile read MN-major
 //          (token rows of 128 channel bytes, as TMA stored it), B = P' rows of 16 bytes: the
 //          four little-endian bytes of p'_h = round(p_h * v_scale_t * 2^Ev) < 2^32.
+//          INT4: value bytes pack tokens 2p (lo) and 2p + 1 (hi); as for the keys, two MMAs
+//          read the packed pair rows against rows of v_p = round(p'_2p+1 / 16) and two read a
+//          low-nibble copy against rows of p'_2p - v_p, both as balanced signed bytes
+//          (p' < 2^30).
 //          O_h = D_pv combined over limbs * 2^-Ev + sum_t p_h v_zero_t          (fp32)
 //
 // Thread t owns token t for the softmax (no redundancy: its 4 heads are 4 registers) and
@@ -40,7 +49,7 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
   return uint64_t((addr >> 4) & 0x3FFFu) | (uint64_t((lbo >> 4) & 0x3FFFu) << 16) |
          (uint64_t((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (uint64_t(layout) << 61);
 }
-constexpr uint32_t kSw128 = 2, kSwNone = 0;
+constexpr uint32_t kSw128 = 2, kSw64 = 4, kSwNone = 0;
 
 // instruction descriptor of kind::i8 with an s32 accumulator
 constexpr uint32_t idesc_i8(int m, int n, bool a_signed, bool b_signed, bool a_mn, bool b_mn) {
@@ -119,8 +128,8 @@ struct TCfg {
   static constexpr int K_TILE = CHUNK * K_ROW;
   static constexpr int V_TILE = (INT4 ? CHUNK / 2 : CHUNK) * 128;
   static constexpr int VS_BYTES = CHUNK * 16;               // v_scale [token][8 heads] fp16
-  static constexpr int KX_BYTES = INT4 ? CHUNK * 128 : 0;       // unpacked keys
-  static constexpr int VX_BYTES = INT4 ? CHUNK * 128 : 0;       // unpacked values
+  static constexpr int KX_BYTES = INT4 ? CHUNK * 64 : 0;        // low nibbles of the keys
+  static constexpr int VX_BYTES = INT4 ? CHUNK / 2 * 128 : 0;   // low nibbles of the values
   static constexpr int P_BYTES = CHUNK * 16;                // P' [token][16 B]
   // K slot = key tile + the chunk's k_scale | k_zero rows (nslot x 512 B); V slot = value
   // tile + v_scale and v_zero of the chunk's tokens for the 8 heads around this one
@@ -182,10 +191,13 @@ kivi_tc_decode_kernel(const __grid_constant__ CUtensorMap tmK,
   constexpr int vslot = C::vslot_bytes();
   uint8_t* kring = smem;
   uint8_t* vring = kring + SK * kslot;
-  uint8_t* kx = vring + SV * vslot;                        // INT4 unpacked keys
-  uint8_t* vx = kx + C::KX_BYTES;                          // INT4 unpacked values
-  uint8_t* bqk = vx + C::VX_BYTES;                         // q' limb rows (K-major SW128)
-  uint8_t* pbuf = bqk + C::bqk_bytes(nslot);               // P' [token][16 B]
+  uint8_t* kx = vring + SV * vslot;                        // INT4 low-nibble key tile
+  uint8_t* vx = kx + C::KX_BYTES;                          // INT4 low-nibble value tile
+  // q' limb rows (K-major; INT8 128-byte rows, 128-byte swizzle; INT4 two sets of 64-byte
+  // rows, 64-byte swizzle: v rows for the packed tile, then x - v rows for the low nibbles)
+  uint8_t* bqk = vx + C::VX_BYTES;
+  // P' [token][16 B] (INT4: [pair][16 B] of v for the packed tile, then of p' - v)
+  uint8_t* pbuf = bqk + C::bqk_bytes(nslot);
   uint8_t* misc = pbuf + C::P_BYTES;
   float2* qp = reinterpret_cast<float2*>(misc);            // [slot][head] {bias', kdown'}
   uint32_t* xchg = reinterpret_cast<uint32_t*>(misc + nslot * 32);          // [3][8]
@@ -371,20 +383,23 @@ kivi_tc_decode_kernel(const __grid_constant__ CUtensorMap tmK,
     // ================================================================ MMA warp (lane 0)
     if (lane == 0) {
       const uint32_t id_qk = tc::idesc_i8(128, 16 * nslot, false, true, false, false);
-      const uint32_t id_pv = tc::idesc_i8(128, 16, false, false, true, true);
+      const uint32_t id_pv = tc::idesc_i8(128, 16, false, INT4, true, true);
       auto issue_pv = [&](int cc) {
         if (!mbar_wait(pready, uint32_t(cc) & 1u)) {
           *abort_flag = 1;
           return false;
         }
         tc::fence_after();
-        const uint32_t a0 = smem_u32(INT4 ? vx : vring + (cc % SV) * vslot), b0 = smem_u32(pbuf);
+        const uint32_t a0 = smem_u32(vring + (cc % SV) * vslot), b0 = smem_u32(pbuf);
         const uint32_t acc0 = *pv_reset ? 0u : 1u;
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          tc::mma_i8(tmem + pv_col, tc::smem_desc(a0 + 4096 * k, 16384, 1024, tc::kSw128),
+        for (int k = 0; k < 4; ++k) {
+          // INT4: k = 0, 1 the packed pair rows, k = 2, 3 their low nibbles (32 rows each)
+          const uint32_t a = INT4 ? (k < 2 ? a0 : smem_u32(vx)) + 4096 * (k & 1) : a0 + 4096 * k;
+          tc::mma_i8(tmem + pv_col, tc::smem_desc(a, 16384, 1024, tc::kSw128),
                      tc::smem_desc(b0 + 512 * k, 128, 256, tc::kSwNone), id_pv,
                      k == 0 ? acc0 : 1u);
+        }
         tc::commit(pv_bar);
         tc::commit(&vempty[cc % SV]);
         ++pv_issued;
@@ -397,12 +412,21 @@ kivi_tc_decode_kernel(const __grid_constant__ CUtensorMap tmK,
           break;
         }
         tc::fence_after();
-        const uint32_t a0 = smem_u32(INT4 ? kx : kring + (c % SK) * kslot);
+        const uint32_t a0 = smem_u32(kring + (c % SK) * kslot);
         const uint32_t b0 = smem_u32(bqk);
+        if constexpr (INT4) {   // packed key bytes x v rows, then low nibbles x (x - v) rows
+          const uint32_t a1 = smem_u32(kx), b1 = b0 + uint32_t(nslot) * 16u * 64u;
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          tc::mma_i8(tmem, tc::smem_desc(a0 + 32 * k, 16, 1024, tc::kSw128),
-                     tc::smem_desc(b0 + 32 * k, 16, 1024, tc::kSw128), id_qk, k > 0);
+          for (int k = 0; k < 4; ++k)
+            tc::mma_i8(tmem, tc::smem_desc((k < 2 ? a0 : a1) + 32 * (k & 1), 16, 512, tc::kSw64),
+                       tc::smem_desc((k < 2 ? b0 : b1) + 32 * (k & 1), 16, 512, tc::kSw64),
+                       id_qk, k > 0);
+        } else {
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            tc::mma_i8(tmem, tc::smem_desc(a0 + 32 * k, 16, 1024, tc::kSw128),
+                       tc::smem_desc(b0 + 32 * k, 16, 1024, tc::kSw128), id_qk, k > 0);
+        }
         tc::commit(qk_bar);
         tc::commit(&kempty[c % SK]);
         ++qk_issued;
@@ -441,7 +465,7 @@ kivi_tc_decode_kernel(const __grid_constant__ CUtensorMap tmK,
 
     // the q' limbs of one page slot: 4 channels per lane, this warp's head
     struct Limbs {
-      uint32_t l0, l1, l2;
+      uint32_t l0, l1, l2, l3;   // l3: INT4 only
       float bias, kdown;
     };
     auto quantize = [&](const __half* kpar_j) -> Limbs {
@@ -467,51 +491,77 @@ kivi_tc_decode_kernel(const __grid_constant__ CUtensorMap tmK,
       const uint32_t bm = redux_max_nv(__float_as_uint(fabsf(bp)));
       const int eb = bm ? min(126, 24 - exponent_of_bits(bm)) : 0;
       const float bsum = float(redux_add_s32(__float2int_rn(bp * exp2i(eb)))) * exp2i(-eb);
-      // |q' 2^ek| < 2^22 keeps the top balanced limb inside int8
-      const int ek = qm ? min(126, 21 - exponent_of_bits(qm)) : 0;
+      // |q' 2^ek| < 2^22 keeps the top of three balanced limbs inside int8. INT4 uses four
+      // limbs and |q' 2^ek| < 2^26, so the odd channels' v = round(x / 16) keeps 22 bits.
+      const int ek = qm ? min(126, (INT4 ? 25 : 21) - exponent_of_bits(qm)) : 0;
       const float kup = exp2i(ek);
-      const uint32_t y0 = uint32_t(__float2int_rn(qs0 * kup) + 0x808080);
-      const uint32_t y1 = uint32_t(__float2int_rn(qs1 * kup) + 0x808080);
-      const uint32_t y2 = uint32_t(__float2int_rn(qs2 * kup) + 0x808080);
-      const uint32_t y3 = uint32_t(__float2int_rn(qs3 * kup) + 0x808080);
+      int x0 = __float2int_rn(qs0 * kup), x1 = __float2int_rn(qs1 * kup);
+      int x2 = __float2int_rn(qs2 * kup), x3 = __float2int_rn(qs3 * kup);
+      if constexpr (INT4) {
+        // lanes 16-31 (odd channels): v = round(x / 16), for the packed tile; lanes 0-15 (even
+        // channels of the same pairs): x - v of the partner lane, for the low-nibble tile
+        const float kq = kup * 0.0625f;
+        const int v0 = __float2int_rn(qs0 * kq), v1 = __float2int_rn(qs1 * kq);
+        const int v2 = __float2int_rn(qs2 * kq), v3 = __float2int_rn(qs3 * kq);
+        const int w0 = __shfl_xor_sync(kFullMask, v0, 16), w1 = __shfl_xor_sync(kFullMask, v1, 16);
+        const int w2 = __shfl_xor_sync(kFullMask, v2, 16), w3 = __shfl_xor_sync(kFullMask, v3, 16);
+        const bool lo_lane = lane < 16;
+        x0 = lo_lane ? x0 - w0 : v0;
+        x1 = lo_lane ? x1 - w1 : v1;
+        x2 = lo_lane ? x2 - w2 : v2;
+        x3 = lo_lane ? x3 - w3 : v3;
+      }
+      // x + 0x80808080 (INT4, four limbs) or x + 0x808080 (three limbs) = sum_k (l_k + 128)
+      // 256^k: byte k ^ 0x80 is the signed limb l_k
+      constexpr uint32_t kBias = INT4 ? 0x80808080u : 0x808080u;
+      const uint32_t y0 = uint32_t(x0) + kBias, y1 = uint32_t(x1) + kBias;
+      const uint32_t y2 = uint32_t(x2) + kBias, y3 = uint32_t(x3) + kBias;
       // x + 0x808080 = sum_k (l_k + 128) 256^k: byte k ^ 0x80 is the signed limb l_k
       return Limbs{byte_sel(y0, y1, y2, y3, 0u) ^ 0x80808080u,
                    byte_sel(y0, y1, y2, y3, 1u) ^ 0x80808080u,
-                   byte_sel(y0, y1, y2, y3, 2u) ^ 0x80808080u, bsum * p.scale_log2,
+                   byte_sel(y0, y1, y2, y3, 2u) ^ 0x80808080u,
+                   INT4 ? byte_sel(y0, y1, y2, y3, 3u) ^ 0x80808080u : 0u, bsum * p.scale_log2,
                    exp2i(-ek) * p.scale_log2};
     };
     auto store_limbs = [&](int j, const Limbs& L) {
       const int row0 = 16 * j + 4 * warp;
       const uint32_t cofs = (uint32_t(lane) & 3u) << 2;
-      const uint32_t lv[3] = {L.l0, L.l1, L.l2};
+      const uint32_t lv[4] = {L.l0, L.l1, L.l2, L.l3};
 #pragma unroll
-      for (int limb = 0; limb < 3; ++limb) {
+      for (int limb = 0; limb < (INT4 ? 4 : 3); ++limb) {
         const int row = row0 + limb;
-        *reinterpret_cast<uint32_t*>(bqk + row * 128 + ((uint32_t((lane >> 2) ^ (row & 7))) << 4) +
-                                     cofs) = lv[limb];
+        if constexpr (INT4) {   // pair bytes 4 (lane & 15) .. + 3 of a 64-byte swizzled row
+          uint8_t* set = bqk + (lane < 16 ? nslot * 16 * 64 : 0);
+          const uint32_t chunk = (uint32_t(lane) & 15u) >> 2;
+          *reinterpret_cast<uint32_t*>(set + row * 64 + ((chunk ^ uint32_t((row >> 1) & 3)) << 4) +
+                                       cofs) = lv[limb];
+        } else {
+          *reinterpret_cast<uint32_t*>(bqk + row * 128 +
+                                       ((uint32_t((lane >> 2) ^ (row & 7))) << 4) + cofs) =
+              lv[limb];
+        }
       }
       if (lane == 0) qp[j * 4 + warp] = make_float2(L.bias, L.kdown);
     };
-    // q' limbs of chunk cc against its k_scale rows (INT4: first unpack this token's keys)
+    // low nibbles of a packed INT4 tile, word for word (the copy keeps the tile's layout)
+    auto low_nibbles = [&](const uint8_t* src, uint8_t* dst, int bytes) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int o = 16 * (tid + i * C::CONSUMERS);
+        if (o < bytes) {
+          const uint4 w = *reinterpret_cast<const uint4*>(src + o);
+          *reinterpret_cast<uint4*>(dst + o) = make_uint4(
+              w.x & 0x0F0F0F0Fu, w.y & 0x0F0F0F0Fu, w.z & 0x0F0F0F0Fu, w.w & 0x0F0F0F0Fu);
+        }
+      }
+    };
+    // q' limbs of chunk cc against its k_scale rows (INT4: and the keys' low-nibble tile)
     auto prep = [&](int cc) {
       const uint8_t* kb = kring + (cc % SK) * kslot;
       const __half* kpar = reinterpret_cast<const __half*>(kb + C::K_TILE);
       const int tok0 = (u0 + cc) * CHUNK;
       const int nbox = min(nslot, (t_end - tok0 + R - 1) >> lR);
-      if constexpr (INT4) {   // byte k < 64 <- low nibbles of packed byte k, >= 64 <- high
-        const uint8_t* src = kb + tid * 64;
-        uint8_t* dst = kx + tid * 128;
-#pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-          const uint4 w = *reinterpret_cast<const uint4*>(src + ((c4 ^ ((tid >> 1) & 3)) << 4));
-          const uint4 lo = make_uint4(w.x & 0x0F0F0F0Fu, w.y & 0x0F0F0F0Fu, w.z & 0x0F0F0F0Fu,
-                                      w.w & 0x0F0F0F0Fu);
-          const uint4 hi = make_uint4((w.x >> 4) & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu,
-                                      (w.z >> 4) & 0x0F0F0F0Fu, (w.w >> 4) & 0x0F0F0F0Fu);
-          *reinterpret_cast<uint4*>(dst + ((c4 ^ (tid & 7)) << 4)) = lo;
-          *reinterpret_cast<uint4*>(dst + (((c4 + 4) ^ (tid & 7)) << 4)) = hi;
-        }
-      }
+      if constexpr (INT4) low_nibbles(kb, kx, C::KX_BYTES);
       if (!prep_warp) return;
       for (int j = 0; j < nbox; j += 2) {   // two page slots at a time (independent chains)
         const int j2 = min(j + 1, nbox - 1);
@@ -576,8 +626,9 @@ kivi_tc_decode_kernel(const __grid_constant__ CUtensorMap tmK,
         const float2* qpb = qp + slot * 4;
 #pragma unroll
         for (int hh = 0; hh < 4; ++hh) {
-          const float s = fmaf(65536.f, float(int(r[4 * hh + 2])),
-                               fmaf(256.f, float(int(r[4 * hh + 1])), float(int(r[4 * hh]))));
+          float s = fmaf(65536.f, float(int(r[4 * hh + 2])),
+                         fmaf(256.f, float(int(r[4 * hh + 1])), float(int(r[4 * hh]))));
+          if constexpr (INT4) s = fmaf(16777216.f, float(int(r[4 * hh + 3])), s);
           const float2 q2 = qpb[hh];
           x[hh] = valid ? fmaf(s, q2.y, q2.x) : kNegInf;
         }
@@ -610,23 +661,9 @@ kivi_tc_decode_kernel(const __grid_constant__ CUtensorMap tmK,
       const uint32_t vmb = xc[4];
       if (tid < 8) xchg[((c + 2) % 3) * 8 + tid] = tid < 4 ? tc::kOrdNegInf : 0u;
 
-      // ---- PV of chunk c - 1 done: P' / unpacked values are free, D_pv is final
+      // ---- PV of chunk c - 1 done: P' / the values' low-nibble tile are free, D_pv is final
       if (c >= 1) wait_or_abort(pv_bar, c - 1);
-      if constexpr (INT4) {   // value pair-rows -> token rows (2 p <- low, 2 p + 1 <- high)
-        const int pr = tid >> 1;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int cc = 4 * (tid & 1) + i;
-          const uint4 w = *reinterpret_cast<const uint4*>(vb + pr * 128 + ((cc ^ (pr & 7)) << 4));
-          const uint4 lo = make_uint4(w.x & 0x0F0F0F0Fu, w.y & 0x0F0F0F0Fu, w.z & 0x0F0F0F0Fu,
-                                      w.w & 0x0F0F0F0Fu);
-          const uint4 hi = make_uint4((w.x >> 4) & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu,
-                                      (w.z >> 4) & 0x0F0F0F0Fu, (w.w >> 4) & 0x0F0F0F0Fu);
-          const int t0 = 2 * pr, t1 = 2 * pr + 1;
-          *reinterpret_cast<uint4*>(vx + t0 * 128 + ((cc ^ (t0 & 7)) << 4)) = lo;
-          *reinterpret_cast<uint4*>(vx + t1 * 128 + ((cc ^ (t1 & 7)) << 4)) = hi;
-        }
-      }
+      if constexpr (INT4) low_nibbles(vb, vx, C::VX_BYTES);
 
       // ---- reference max / value exponent (uniform over the CTA); read D_pv back if needed
       bool need[4], m_rebase = false;
@@ -641,7 +678,8 @@ kivi_tc_decode_kernel(const __grid_constant__ CUtensorMap tmK,
         const int ve = 31 - int(kSoftmaxHeadroom) - exponent_of_bits(vmb);
         if (vexp == kExpUnset || ve < vexp) {
           v_rebase = vexp != kExpUnset;
-          vexp_new = max(-126, min(126, ve - kValueHeadroom));
+          // INT4: one more bit, so p' - v stays inside four balanced signed bytes
+          vexp_new = max(-126, min(126, ve - kValueHeadroom - (INT4 ? 1 : 0)));
         }
       }
       if (since_flush > 0 && (m_rebase || v_rebase || since_flush >= 256) && !*cabort) {
@@ -668,9 +706,21 @@ kivi_tc_decode_kernel(const __grid_constant__ CUtensorMap tmK,
         const float pe = fast_exp2(x[hh] - (m_ref[hh] == kNegInf ? 0.f : m_ref[hh]));
         l_run[hh] += pe;
         z_run[hh] = fmaf(pe, vz, z_run[hh]);
-        pq[hh] = __float2uint_rn(pe * vsup);   // saturates at 2^32 - 1
+        if constexpr (INT4) {
+          // pair p = tokens 2p (thread 2p) and 2p + 1: the odd token's v = round(p' / 16) goes
+          // to the packed tile's row p, the even token's p' - v to the low-nibble tile's row p,
+          // both as balanced signed bytes (x + 0x80808080: byte ^ 0x80 is the signed limb)
+          const float pv = pe * vsup;
+          const int v = __float2int_rn(pv * 0.0625f);
+          const int w = __shfl_xor_sync(kFullMask, v, 1);
+          const int x = (tid & 1) ? v : __float2int_rn(pv) - w;
+          pq[hh] = (uint32_t(x) + 0x80808080u) ^ 0x80808080u;
+        } else {
+          pq[hh] = __float2uint_rn(pe * vsup);   // saturates at 2^32 - 1
+        }
       }
-      *reinterpret_cast<uint4*>(pbuf + 16 * tid) = make_uint4(pq[0], pq[1], pq[2], pq[3]);
+      uint8_t* prow = INT4 ? pbuf + ((tid & 1) ? 0 : 1024) + 16 * (tid >> 1) : pbuf + 16 * tid;
+      *reinterpret_cast<uint4*>(prow) = make_uint4(pq[0], pq[1], pq[2], pq[3]);
       if (tid == 0) *pv_reset = reset_pv ? 1 : 0;
       tc::fence_async_smem();
       tc::fence_before();
