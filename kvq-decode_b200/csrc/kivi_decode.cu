@@ -722,9 +722,23 @@ int launch(const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tks,
 #ifndef BPT_KIVI_TC_MINB
 #define BPT_KIVI_TC_MINB 2
 #endif
+// INT4 at large batch uses a second tcgen05 shape: a 2-slot value ring, which fits 3 CTAs per
+// SM. Measured on one B200: INT4 B=64/32k 928 -> 872 us, but B=1/128k 64.9 -> 67.6 us (more
+// splits, fewer chunks per CTA). It serves calls with batch * kv_heads >= this many CTAs.
+#ifndef BPT_KIVI_TC_WIDE_MIN_CTAS
+#define BPT_KIVI_TC_WIDE_MIN_CTAS 256
+#endif
 
-template <int FMT>
-using TcCfg = TCfg<FMT, BPT_KIVI_TC_KSLOTS, BPT_KIVI_TC_VSLOTS>;
+template <int FMT, bool WIDE = false>
+using TcCfg = TCfg<FMT, BPT_KIVI_TC_KSLOTS, WIDE ? 2 : BPT_KIVI_TC_VSLOTS>;
+template <bool WIDE>
+constexpr int tc_minb() {
+  return WIDE ? 3 : BPT_KIVI_TC_MINB;
+}
+
+inline bool tc_wide(int format, int batch, int kv_heads) {
+  return format == BPT_KV_INT4 && int64_t(batch) * kv_heads >= BPT_KIVI_TC_WIDE_MIN_CTAS;
+}
 
 template <int FMT>
 using IntCfg =
@@ -743,23 +757,23 @@ int int_resident_ctas(int block_size) {
   return r < 1 ? 1 : r;
 }
 
-template <int FMT>
+template <int FMT, bool WIDE = false>
 int tc_resident_ctas(int block_size) {
-  using C = TcCfg<FMT>;
+  using C = TcCfg<FMT, WIDE>;
   const int box = block_size < C::CHUNK ? block_size : C::CHUNK;
   const int per = int(C::smem_bytes(C::CHUNK / box)) + kSmemPerCtaReserved;
   int r = kSmemPerSm / per;
-  if (r > BPT_KIVI_TC_MINB) r = BPT_KIVI_TC_MINB;
+  if (r > tc_minb<WIDE>()) r = tc_minb<WIDE>();
   return r < 1 ? 1 : r;
 }
 
-template <int FMT>
+template <int FMT, bool WIDE = false>
 int launch_tc(const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tks,
               const CUtensorMap& tkz, const CUtensorMap& tvs, const CUtensorMap& tvz,
               const KiviParams& kp, cudaStream_t st) {
-  using C = TcCfg<FMT>;
-  auto kern = kivi_tc_decode_kernel<FMT, BPT_KIVI_TC_KSLOTS, BPT_KIVI_TC_VSLOTS,
-                                    BPT_KIVI_TC_MINB>;
+  using C = TcCfg<FMT, WIDE>;
+  auto kern = kivi_tc_decode_kernel<FMT, BPT_KIVI_TC_KSLOTS, WIDE ? 2 : BPT_KIVI_TC_VSLOTS,
+                                    tc_minb<WIDE>()>;
   const size_t smem = C::smem_bytes(C::CHUNK / kp.d.box_rows);
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) !=
       cudaSuccess)
@@ -847,15 +861,16 @@ KiviKernel kivi_kernel_for(int format, int group, int block_size, int kv_heads) 
 }
 
 // tokens per pipeline stage and CTAs per SM of the kernel serving (format, group)
-void kivi_kernel_shape(int format, int group, int block_size, int kv_heads, int* chunk,
-                       int* resident) {
+void kivi_kernel_shape(int format, int group, int block_size, int kv_heads, int batch,
+                       int* chunk, int* resident) {
   using namespace kivi;
   const bool int4 = format == BPT_KV_INT4;
   switch (kivi_kernel_for(format, group, block_size, kv_heads)) {
     case KiviKernel::TC:
       *chunk = TcCfg<BPT_KV_INT8>::CHUNK;
-      *resident = int4 ? tc_resident_ctas<BPT_KV_INT4>(block_size)
-                       : tc_resident_ctas<BPT_KV_INT8>(block_size);
+      *resident = !int4 ? tc_resident_ctas<BPT_KV_INT8>(block_size)
+                  : tc_wide(format, batch, kv_heads) ? tc_resident_ctas<BPT_KV_INT4, true>(block_size)
+                                                     : tc_resident_ctas<BPT_KV_INT4>(block_size);
       break;
     case KiviKernel::INT:
       *chunk = IntCfg<BPT_KV_INT8>::CHUNK;
@@ -874,7 +889,7 @@ int effective_splits_kivi(int format, int batch, int kv_heads, int q_heads, int 
                           int max_blocks, int num_splits, int sm_count) {
   const int group = (kv_heads > 0 && q_heads > 0) ? q_heads / kv_heads : 1;
   int chunk, resident;
-  kivi_kernel_shape(format, group, block_size, kv_heads, &chunk, &resident);
+  kivi_kernel_shape(format, group, block_size, kv_heads, batch, &chunk, &resident);
   const int s = num_splits > 0 ? num_splits
                                : plan_splits(batch, kv_heads, block_size, max_blocks, sm_count,
                                              resident, chunk);
@@ -980,8 +995,12 @@ int run_split_kivi(const bpt_kivi_cache& c, const void* q, int64_t q_sb, int64_t
       rc = encode_vparam_map(&tvz, c.v_zero, c.kv_heads, bs, c.num_blocks, c.v_param_stride[0],
                              c.v_param_stride[1], box_rows);
       if (rc) return rc;
-      rc = int4 ? launch_tc<BPT_KV_INT4>(tk, tv, tks, tkz, tvs, tvz, kp, st)
-                : launch_tc<BPT_KV_INT8>(tk, tv, tks, tkz, tvs, tvz, kp, st);
+      if (!int4)
+        rc = launch_tc<BPT_KV_INT8>(tk, tv, tks, tkz, tvs, tvz, kp, st);
+      else if (tc_wide(c.format, batch, c.kv_heads))
+        rc = launch_tc<BPT_KV_INT4, true>(tk, tv, tks, tkz, tvs, tvz, kp, st);
+      else
+        rc = launch_tc<BPT_KV_INT4>(tk, tv, tks, tkz, tvs, tvz, kp, st);
     } else
       rc = int4 ? launch_int<BPT_KV_INT4>(tk, tv, tks, tkz, kp, st)
                 : launch_int<BPT_KV_INT8>(tk, tv, tks, tkz, kp, st);

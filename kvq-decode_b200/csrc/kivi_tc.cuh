@@ -140,10 +140,10 @@ struct TCfg {
     return (V_TILE + 2 * VS_BYTES + 1023) & ~1023;
   }
   __host__ __device__ static constexpr int bqk_bytes(int nslot) { return nslot * 16 * 128; }
-  // misc: qp [slot][head] float2 | xchg [3][8] | reduce [4][8] | tmem slot, abort flags,
-  // pv reset flag | mbarriers
+  // misc: qp [chunk parity][slot][head] float2 | xchg [3][8] | reduce [4][8] | tmem slot,
+  // abort flags, pv reset flag | mbarriers
   __host__ __device__ static constexpr int misc_bytes(int nslot) {
-    return nslot * 32 + 96 + 128 + 32 + (2 * SK + 2 * SV + 4) * 8;
+    return 2 * nslot * 32 + 96 + 128 + 32 + (2 * SK + 2 * SV + 4) * 8;
   }
   __host__ __device__ static constexpr size_t smem_bytes(int nslot) {
     return 1024 + size_t(SK) * kslot_bytes(nslot) + size_t(SV) * vslot_bytes() + KX_BYTES +
@@ -199,16 +199,21 @@ kivi_tc_decode_kernel(const __grid_constant__ CUtensorMap tmK,
   // P' [token][16 B] (INT4: [pair][16 B] of v for the packed tile, then of p' - v)
   uint8_t* pbuf = bqk + C::bqk_bytes(nslot);
   uint8_t* misc = pbuf + C::P_BYTES;
-  float2* qp = reinterpret_cast<float2*>(misc);            // [slot][head] {bias', kdown'}
-  uint32_t* xchg = reinterpret_cast<uint32_t*>(misc + nslot * 32);          // [3][8]
-  float* red = reinterpret_cast<float*>(misc + nslot * 32 + 96);             // [4 warps][8]
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(misc + nslot * 32 + 224);
+  // {bias', kdown'} per [chunk parity][slot][head]: every compute warp reads all heads' entries
+  // of chunk c for its scores while a faster warp may already write chunk c + 1's, so the two
+  // chunks use different halves (a warp reaches chunk c + 2 only after the named barrier that
+  // every warp passes after its chunk-c score read)
+  float2* qp = reinterpret_cast<float2*>(misc);
+  const int qp_bytes = 2 * nslot * 32;
+  uint32_t* xchg = reinterpret_cast<uint32_t*>(misc + qp_bytes);          // [3][8]
+  float* red = reinterpret_cast<float*>(misc + qp_bytes + 96);             // [4 warps][8]
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(misc + qp_bytes + 224);
   // abort_flag: any role gave up waiting (producer and MMA warp stop); cabort: written by the
   // compute warps only, read by them right after their named barrier
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + nslot * 32 + 228);
-  volatile int* cabort = reinterpret_cast<volatile int*>(misc + nslot * 32 + 232);
-  volatile int* pv_reset = reinterpret_cast<volatile int*>(misc + nslot * 32 + 236);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(misc + nslot * 32 + 256);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + qp_bytes + 228);
+  volatile int* cabort = reinterpret_cast<volatile int*>(misc + qp_bytes + 232);
+  volatile int* pv_reset = reinterpret_cast<volatile int*>(misc + qp_bytes + 236);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(misc + qp_bytes + 256);
   uint64_t* kfull = bars;                 // producer -> consumers / MMA (TMA bytes)
   uint64_t* kempty = kfull + SK;          // QK committed -> producer
   uint64_t* vfull = kempty + SK;          // TMA bytes
@@ -258,7 +263,7 @@ kivi_tc_decode_kernel(const __grid_constant__ CUtensorMap tmK,
   // q' limb rows start at zero (rows of heads >= group and limb row 3 stay zero)
   for (int i = tid; i < C::bqk_bytes(nslot) / 16; i += blockDim.x)
     reinterpret_cast<uint4*>(bqk)[i] = make_uint4(0u, 0u, 0u, 0u);
-  for (int i = tid; i < nslot * 4; i += blockDim.x) qp[i] = make_float2(0.f, 0.f);
+  for (int i = tid; i < 2 * nslot * 4; i += blockDim.x) qp[i] = make_float2(0.f, 0.f);
   if (tid < 24) xchg[tid] = (tid & 7) < 4 ? tc::kOrdNegInf : 0u;
   if (tid == 0) {
     *abort_flag = 0;
@@ -523,7 +528,7 @@ kivi_tc_decode_kernel(const __grid_constant__ CUtensorMap tmK,
                    INT4 ? byte_sel(y0, y1, y2, y3, 3u) ^ 0x80808080u : 0u, bsum * p.scale_log2,
                    exp2i(-ek) * p.scale_log2};
     };
-    auto store_limbs = [&](int j, const Limbs& L) {
+    auto store_limbs = [&](int j, int cc, const Limbs& L) {
       const int row0 = 16 * j + 4 * warp;
       const uint32_t cofs = (uint32_t(lane) & 3u) << 2;
       const uint32_t lv[4] = {L.l0, L.l1, L.l2, L.l3};
@@ -541,7 +546,7 @@ kivi_tc_decode_kernel(const __grid_constant__ CUtensorMap tmK,
               lv[limb];
         }
       }
-      if (lane == 0) qp[j * 4 + warp] = make_float2(L.bias, L.kdown);
+      if (lane == 0) qp[((cc & 1) * nslot + j) * 4 + warp] = make_float2(L.bias, L.kdown);
     };
     // low nibbles of a packed INT4 tile, word for word (the copy keeps the tile's layout)
     auto low_nibbles = [&](const uint8_t* src, uint8_t* dst, int bytes) {
@@ -567,8 +572,8 @@ kivi_tc_decode_kernel(const __grid_constant__ CUtensorMap tmK,
         const int j2 = min(j + 1, nbox - 1);
         const Limbs a = quantize(kpar + j * 256);
         const Limbs c2 = quantize(kpar + j2 * 256);
-        store_limbs(j, a);
-        if (j2 != j) store_limbs(j2, c2);
+        store_limbs(j, cc, a);
+        if (j2 != j) store_limbs(j2, cc, c2);
       }
     };
 
@@ -623,7 +628,7 @@ kivi_tc_decode_kernel(const __grid_constant__ CUtensorMap tmK,
         uint32_t r[16];
         tc::ld16(tmem_warp + 16u * uint32_t(slot), r);
         const bool valid = tok0 + tid < t_end;
-        const float2* qpb = qp + slot * 4;
+        const float2* qpb = qp + ((c & 1) * nslot + slot) * 4;
 #pragma unroll
         for (int hh = 0; hh < 4; ++hh) {
           float s = fmaf(65536.f, float(int(r[4 * hh + 2])),

@@ -187,3 +187,30 @@ def test_decode_with_fp16_residual(fmt):
     for ns in (None, 1):
         out = paged_decode_attention_kivi_with_residual(*args, num_splits=ns)
         assert_close(out.float().cpu().numpy(), ref, what=f"{fmt} residual ns={ns}")
+
+
+@pytest.mark.parametrize("fmt,B", [("int4", 64), ("int4", 32), ("int8", 32)])
+def test_full_size_decode_is_deterministic(fmt, B):
+    """Repeated calls give bitwise-identical outputs at several split counts. The compute warps
+    share per-page q scale entries in shared memory; a warp that raced ahead into the next
+    chunk must not overwrite the entries another warp is still reading (an earlier version did,
+    rarely, at some split counts)."""
+    from bpt.cache import ragged_lengths
+    from bpt.quant import empty_kivi_cache, paged_decode_attention_kivi, quantize_append
+    ctx, bs, Hq, Hkv, D = 32768, 64, 32, 8, 128
+    lens = ragged_lengths(B, ctx, seed=3)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    k = torch.randn(B, ctx, Hkv, D, device="cuda", generator=g, dtype=torch.float16)
+    v = torch.randn(B, ctx, Hkv, D, device="cuda", generator=g, dtype=torch.float16)
+    q = torch.randn(B, Hq, D, device="cuda", generator=g, dtype=torch.float16)
+    pages = ctx // bs
+    bt = torch.randperm(B * pages, device="cuda").reshape(B, pages).to(torch.int32)
+    cache = empty_kivi_cache(B * pages, bs, Hkv, D, fmt)
+    sl = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    quantize_append(cache, k, v, sl, torch.zeros_like(sl), bt)
+    del k, v
+    for ns in (None, 1, 5, 7):
+        first = paged_decode_attention_kivi(q, cache, bt, sl, num_splits=ns)
+        for _ in range(4):
+            assert torch.equal(first, paged_decode_attention_kivi(q, cache, bt, sl, num_splits=ns)), \
+                f"{fmt} B={B} num_splits={ns}: outputs differ between calls"
