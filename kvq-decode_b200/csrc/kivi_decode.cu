@@ -722,11 +722,16 @@ int launch(const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tks,
 #ifndef BPT_KIVI_TC_MINB
 #define BPT_KIVI_TC_MINB 2
 #endif
-// INT4 at large batch uses a second tcgen05 shape: a 2-slot value ring, which fits 3 CTAs per
-// SM. Measured on one B200: INT4 B=64/32k 928 -> 872 us, but B=1/128k 64.9 -> 67.6 us (more
-// splits, fewer chunks per CTA). It serves calls with batch * kv_heads >= this many CTAs.
+// INT4 at large batch and long context uses a second tcgen05 shape: a 2-slot value ring, which
+// fits 3 CTAs per SM. Measured on one B200: INT4 B=64/32k 929 -> 882 us, B=32/32k 506 ->
+// 490 us; but B=1/128k 64.9 -> 67.6 us and B=32/8k ~181 -> 209 us (more splits, so fewer
+// chunks per CTA to amortise its setup). It serves calls with batch * kv_heads >= MIN_CTAS
+// and a block table of at least MIN_TOKENS tokens.
 #ifndef BPT_KIVI_TC_WIDE_MIN_CTAS
 #define BPT_KIVI_TC_WIDE_MIN_CTAS 256
+#endif
+#ifndef BPT_KIVI_TC_WIDE_MIN_TOKENS
+#define BPT_KIVI_TC_WIDE_MIN_TOKENS 32768
 #endif
 
 template <int FMT, bool WIDE = false>
@@ -736,8 +741,9 @@ constexpr int tc_minb() {
   return WIDE ? 3 : BPT_KIVI_TC_MINB;
 }
 
-inline bool tc_wide(int format, int batch, int kv_heads) {
-  return format == BPT_KV_INT4 && int64_t(batch) * kv_heads >= BPT_KIVI_TC_WIDE_MIN_CTAS;
+inline bool tc_wide(int format, int batch, int kv_heads, int block_size, int max_blocks) {
+  return format == BPT_KV_INT4 && int64_t(batch) * kv_heads >= BPT_KIVI_TC_WIDE_MIN_CTAS &&
+         int64_t(max_blocks) * block_size >= BPT_KIVI_TC_WIDE_MIN_TOKENS;
 }
 
 template <int FMT>
@@ -862,15 +868,16 @@ KiviKernel kivi_kernel_for(int format, int group, int block_size, int kv_heads) 
 
 // tokens per pipeline stage and CTAs per SM of the kernel serving (format, group)
 void kivi_kernel_shape(int format, int group, int block_size, int kv_heads, int batch,
-                       int* chunk, int* resident) {
+                       int max_blocks, int* chunk, int* resident) {
   using namespace kivi;
   const bool int4 = format == BPT_KV_INT4;
   switch (kivi_kernel_for(format, group, block_size, kv_heads)) {
     case KiviKernel::TC:
       *chunk = TcCfg<BPT_KV_INT8>::CHUNK;
       *resident = !int4 ? tc_resident_ctas<BPT_KV_INT8>(block_size)
-                  : tc_wide(format, batch, kv_heads) ? tc_resident_ctas<BPT_KV_INT4, true>(block_size)
-                                                     : tc_resident_ctas<BPT_KV_INT4>(block_size);
+                  : tc_wide(format, batch, kv_heads, block_size, max_blocks)
+                      ? tc_resident_ctas<BPT_KV_INT4, true>(block_size)
+                      : tc_resident_ctas<BPT_KV_INT4>(block_size);
       break;
     case KiviKernel::INT:
       *chunk = IntCfg<BPT_KV_INT8>::CHUNK;
@@ -889,7 +896,7 @@ int effective_splits_kivi(int format, int batch, int kv_heads, int q_heads, int 
                           int max_blocks, int num_splits, int sm_count) {
   const int group = (kv_heads > 0 && q_heads > 0) ? q_heads / kv_heads : 1;
   int chunk, resident;
-  kivi_kernel_shape(format, group, block_size, kv_heads, batch, &chunk, &resident);
+  kivi_kernel_shape(format, group, block_size, kv_heads, batch, max_blocks, &chunk, &resident);
   const int s = num_splits > 0 ? num_splits
                                : plan_splits(batch, kv_heads, block_size, max_blocks, sm_count,
                                              resident, chunk);
@@ -997,7 +1004,7 @@ int run_split_kivi(const bpt_kivi_cache& c, const void* q, int64_t q_sb, int64_t
       if (rc) return rc;
       if (!int4)
         rc = launch_tc<BPT_KV_INT8>(tk, tv, tks, tkz, tvs, tvz, kp, st);
-      else if (tc_wide(c.format, batch, c.kv_heads))
+      else if (tc_wide(c.format, batch, c.kv_heads, bs, max_blocks))
         rc = launch_tc<BPT_KV_INT4, true>(tk, tv, tks, tkz, tvs, tvz, kp, st);
       else
         rc = launch_tc<BPT_KV_INT4>(tk, tv, tks, tkz, tvs, tvz, kp, st);

@@ -71,9 +71,11 @@ def test_kivi_planner_uses_the_serving_kernels_shape():
     # FP8 and group 8 stay on the fp16-MMA kernel: 4 CTAs per SM, 32-token stages
     assert f(FP8, 1, 8, 32, 64, 2048, 0, 148) == 74
     assert f(INT4, 1, 8, 64, 64, 2048, 0, 148) == 74
-    # INT4 with batch x kv_heads >= 256 uses the 3-CTA/SM tcgen05 shape (more splits than INT8)
+    # INT4 with batch x kv_heads >= 256 and a block table of >= 32k tokens uses the 3-CTA/SM
+    # tcgen05 shape (more splits than INT8); shorter tables and smaller batches keep 2 per SM
     assert f(INT4, 64, 8, 32, 64, 512, 0, 148) == 7
     assert f(INT4, 32, 8, 32, 64, 512, 0, 148) == 14
+    assert f(INT4, 32, 8, 32, 64, 128, 0, 148) == 10
     assert f(INT8, 64, 8, 32, 64, 512, 0, 148) == 5
     assert f(INT4, 8, 8, 32, 64, 512, 0, 148) == 4
     # explicit requests are clamped to the 128-token chunk count
