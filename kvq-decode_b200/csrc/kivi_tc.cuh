@@ -15,7 +15,7 @@
 //          limbs, |x| < 2^26, so v keeps 22 bits). Two MMAs read the
 //          packed tile as TMA stored it (64-byte rows, 64-byte swizzle) against B rows of v,
 //          two read a low-nibble copy (one AND per word, same layout) against rows of x_2k - v.
-//          S_h = (L0 + 256 L1 + 65536 L2) * 2^-Ek + sum_d q_d k_zero_d            (fp32)
+//          S_h = (L0 + 256 L1 + 65536 L2 [+ 2^24 L3, INT4]) * 2^-Ek + sum_d q_d k_zero_d
 //   P.V    D_pv[channel][4 h + limb] += sum_t V[t][channel] * P'[t][4 h + limb]
 //          M = 128 channels, N = 16, K = 128 tokens. A = the value code tile read MN-major
 //          (token rows of 128 channel bytes, as TMA stored it), B = P' rows of 16 bytes: the
@@ -37,10 +37,12 @@
 // [token][8 heads] v_scale / v_zero rows around this head), warp 5 issues the MMAs. Keys and
 // values have separate TMA rings (SK / SV slots); a slot is refilled when the MMA that read it
 // committed (tcgen05.commit on the slot's "empty" barrier). Per chunk c the compute warps read
-// S(c) from TMEM, quantize q for chunk c + 1 (INT4: unpack its keys) and publish it (QK(c + 1)
-// overlaps the rest of the chunk), exchange chunk maxima, then (PV(c - 1) done) write P'(c)
-// (INT4: unpack chunk c's values) for PV(c). Every wait on TMA / MMA completion or on another
-// warp is time-bounded; a failed wait raises a shared abort flag.
+// S(c) from TMEM, quantize q for chunk c + 1 (INT4: and copy its keys' low nibbles) and
+// publish it (QK(c + 1) overlaps the rest of the chunk), exchange chunk maxima, then
+// (PV(c - 1) done) write P'(c) (INT4: and chunk c's value low nibbles) for PV(c). INT4 calls
+// at large batch and long context use a 2-slot value ring (3 CTAs per SM). Every wait on
+// TMA / MMA completion or on another warp is time-bounded; a failed wait raises a shared
+// abort flag.
 
 namespace tc {
 
