@@ -2,7 +2,7 @@
 
 Run in a container where the reference checkout is present:
 
-    python tests/golden/make_golden.py [--reference-dir DIR]
+    python tests/golden/make_golden.py --reference-dir DIR   (or BPT_REFERENCE_DIR=DIR)
 
 It loads ``src/bpt/reference.py`` of the reference by file path (the new package is also
 called ``bpt``, so a normal import would collide), builds every case's inputs with the seeded
@@ -120,9 +120,11 @@ def run_reference(ref, q, kc, vc, bt, sl):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference-dir", default=os.environ.get("BPT_REFERENCE_DIR",
-                                                              "/root/reference"))
+    ap.add_argument("--reference-dir", default=os.environ.get("BPT_REFERENCE_DIR"),
+                    help="checkout of the reference project (or set BPT_REFERENCE_DIR)")
     args = ap.parse_args()
+    if not args.reference_dir:
+        ap.error("give --reference-dir or set BPT_REFERENCE_DIR")
     ref = load_reference(args.reference_dir)
     import torch
     torch.set_num_threads(os.cpu_count() or 1)
