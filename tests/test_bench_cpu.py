@@ -40,6 +40,24 @@ def test_reference_arm_json_line():
     assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
 
 
+def test_reference_arm_under_torchrun_prints_once():
+    """Launched like the driver's N-GPU runs: rank 0 alone runs and prints one line, the other
+    ranks exit 0 without work."""
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+                        "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port",
+                        str(port), os.path.join(ROOT, "bench.py"), "--impl", "reference",
+                        "--gpus", "2", "--workload", "fp16_b1_ctx4k", "--steps", "1",
+                        "--warmup", "0"], cwd=ROOT, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1, r.stdout
+    assert json.loads(lines[0])["impl"] == "reference"
+
+
 @pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-GPU failure path")
 def test_product_arm_fails_without_gpu():
     r = _run("--steps", "1", "--warmup", "0", timeout=120)
