@@ -192,10 +192,13 @@ int bpt_decode_kivi_partial(const bpt_kivi_cache* cache,
  * No counterpart in the reference. The split-KV partial states live in a fixed
  * BPT_NOALLOC_SCRATCH_BYTES array inside the library, reserved on each GPU that loads it until
  * the process exits; a call needing more (B * Hq * splits * (head_dim + 1) * 4 bytes, rounded)
- * returns BPT_ERR_WORKSPACE_TOO_SMALL without launching. The first call on a device looks up
- * that device's array address (cudaGetSymbolAddress, with the device current); make it before
+ * returns BPT_ERR_WORKSPACE_TOO_SMALL without launching. Every call made outside stream
+ * capture looks up the current device's array address (cudaGetSymbolAddress, with the device
+ * current) and keeps it for calls being captured, so make the first call on a device before
  * any stream capture. All calls share the array: calls whose kernels overlap on the GPU race.
- * It allocates nothing and records no device-check flags. Other arguments as bpt_decode_fp16. */
+ * It allocates nothing and records no device-check flags: a block id outside [0, num_blocks)
+ * reads page 0 instead and a too-long seq_len is cut at the table, with no error returned (the
+ * kernels' own guards keep every access in bounds). Other arguments as bpt_decode_fp16. */
 int bpt_decode_fp16_noalloc(const void* q, int64_t q_sb, int64_t q_sh,
                             const void* k_cache, int64_t k_sb, int64_t k_st, int64_t k_sh,
                             const void* v_cache, int64_t v_sb, int64_t v_st, int64_t v_sh,
@@ -219,7 +222,9 @@ int bpt_decode_fp16_noalloc(const void* q, int64_t q_sb, int64_t q_sh,
  * (time-bounded, budget_us) for all ranks' states and writes the merged fp16 out [B, Hq, D] on
  * every rank. bufs[r] is rank r's buffer as mapped in this process (bufs[rank] = own). All
  * ranks must make the same sequence of calls with the same batch / q_heads / head_dim; a wait
- * that runs out sets BPT_DEV_WAIT_TIMEOUT in *status. head_dim % 4 == 0, <= 256; world <= 8. */
+ * that runs out sets BPT_DEV_WAIT_TIMEOUT in *status. head_dim % 4 == 0, <= 256; world <= 8.
+ * The first bpt_seqx_merge_fp16 call on a device sizes the kernel's grid to what is resident
+ * on that device (an occupancy query); make it before capturing the call in a CUDA graph. */
 #define BPT_IPC_HANDLE_BYTES 64
 size_t bpt_seqx_buffer_bytes(int world, int batch, int q_heads, int head_dim);
 int bpt_seqx_alloc(size_t bytes, void** buf, void* ipc_handle);

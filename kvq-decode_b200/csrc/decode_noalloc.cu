@@ -9,9 +9,9 @@
 //
 // The array (BPT_NOALLOC_SCRATCH_BYTES) is reserved on every GPU that loads this library's
 // device code and stays there until the process exits. Host code cannot use the array's name
-// as a device address, so the first call on each device, with that device current, looks the
-// address up with cudaGetSymbolAddress and caches it; make that first call before any stream
-// capture. Every call shares the one array per device, so two calls whose kernels overlap on
+// as a device address, so each call made outside stream capture, with its device current, looks
+// the address up with cudaGetSymbolAddress and keeps it for captured calls; make the first
+// call on each device before any stream capture. Every call shares the one array per device, so two calls whose kernels overlap on
 // the GPU (different streams, no ordering between them) race on it. Nothing in the array needs
 // to start at zero: a call writes every partial-state row it later reads. This path records no
 // device-side check flags (it has no status word to hand back).
@@ -33,18 +33,25 @@ std::mutex g_scratch_mu;
 
 size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
 
-// Device address of this device's copy of the scratch array (looked up once per device).
-int scratch_address(void** addr) {
+// Device address of the current device's copy of the scratch array. Outside stream capture
+// it is looked up on every call, so a reset device or another context made current on the
+// same ordinal (both reload the module, which can move the array) gets its own address; a
+// call being captured reuses the address the last uncaptured call on this device found.
+int scratch_address(cudaStream_t stream, void** addr) {
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
     return BPT_ERR_NO_DEVICE;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  const bool capturing =
+      cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone;
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (!g_scratch_addr[dev]) {
+  if (!capturing) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr)
       return BPT_ERR_LAUNCH;
     g_scratch_addr[dev] = p;
   }
+  if (!g_scratch_addr[dev]) return BPT_ERR_LAUNCH;  // first call on this device was captured
   *addr = g_scratch_addr[dev];
   return BPT_OK;
 }
@@ -76,12 +83,12 @@ extern "C" int bpt_decode_fp16_noalloc(const void* q, int64_t q_sb, int64_t q_sh
   const size_t lse_bytes = round256(rows * sizeof(float));
   if (lse_bytes + rows * head_dim * sizeof(float) > BPT_NOALLOC_SCRATCH_BYTES)
     return BPT_ERR_WORKSPACE_TOO_SMALL;  // more partial state than the fixed array holds
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
   void* base = nullptr;
-  int rc = scratch_address(&base);
+  int rc = scratch_address(st, &base);
   if (rc) return rc;
   float* lse = static_cast<float*>(base);
   float* o_part = reinterpret_cast<float*>(static_cast<char*>(base) + lse_bytes);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   rc = run_split_fp16(q, q_sb, q_sh, k_cache, k_sb, k_st, k_sh, v_cache, v_sb, v_st, v_sh,
                       num_blocks, block_table, bt_sb, seq_lens, out, o_sb, o_sh, batch, q_heads,
                       kv_heads, head_dim, block_size, max_blocks, scale, S, 1, o_part, lse,

@@ -36,6 +36,8 @@
 // the GPU stays usable).
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+
+#include <mutex>
 #include <math.h>
 #include <string.h>
 
@@ -251,16 +253,25 @@ seq_exchange_kernel(const float* __restrict__ o_part, const float* __restrict__ 
   }
 }
 
+// CTAs of the exchange kernel that are resident at once on the current device, cached per
+// device ordinal (GPUs of one process may differ in SM count). The first call on a device
+// queries the occupancy API, so make it before any stream capture.
+constexpr int kMaxGridDevices = 64;
+int g_resident_grid[kMaxGridDevices];
+std::mutex g_resident_mu;
+
 int resident_grid() {
-  static int cached = 0;
-  if (cached) return cached;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxGridDevices) return 0;
+  std::lock_guard<std::mutex> lock(g_resident_mu);
+  if (g_resident_grid[dev]) return g_resident_grid[dev];
   int per_sm = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, seq_exchange_kernel, kThreads,
                                                     0) != cudaSuccess ||
       per_sm < 1)
     per_sm = 1;
-  cached = per_sm * device_sm_count();
-  return cached;
+  g_resident_grid[dev] = per_sm * device_sm_count();
+  return g_resident_grid[dev];
 }
 
 }  // namespace
@@ -332,6 +343,7 @@ extern "C" int bpt_seqx_merge_fp16(const float* o_part, const float* lse, int ba
   }
   const int items = batch * q_heads;
   int grid = resident_grid();
+  if (grid < 1) return BPT_ERR_NO_DEVICE;
   if (grid > items) grid = items;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);

@@ -1,7 +1,8 @@
 """bench.py's JSON contract, checked on the CPU.
 
-* `--impl reference` (the reference's algorithm, the numpy oracle port, timed on the host
-  cores) prints one JSON line with the keys the driver reads: impl, metric, value, unit,
+* `--impl reference` (the reference's own CPU path -- its torch oracle from the offline install
+  under baseline/_ref, or the numpy port when that is absent -- timed on the host cores on
+  whole sequences of the workload) prints one JSON line with the keys the driver reads: impl, metric, value, unit,
   steps / warmup, higher_is_better, config.workload, a cpu_baseline describing the run, and an
   e2e object with zero host<->device bytes.
 * The product arm has no CPU fallback: without a GPU it exits non-zero.
@@ -34,7 +35,10 @@ def test_reference_arm_json_line():
     assert d["value"] > 0 and d["ms_per_step"] > 0
     assert d["config"]["workload"].startswith("fp16_b1_ctx4k")
     cb = d["cpu_baseline"]
-    assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == d["value"] and cb["sample"]
+    installed = os.path.exists(os.path.join(ROOT, "baseline", "_ref", "bpt", "reference.py"))
+    assert cb["kind"] == ("reference" if installed else "port")
+    assert cb["cores"] >= 1 and cb["value"] == d["value"] and cb["sample"]
+    assert "[4096] tokens" in cb["sample"], "whole sequences at their true length"
     e2e = d["e2e"]
     assert e2e["value"] == d["value"] and e2e["unit"] == d["unit"]
     assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0

@@ -14,7 +14,7 @@ import numpy as np
 import pytest
 import torch
 
-from helpers import assert_close, build_fp16, golden_arrays, golden_meta
+from helpers import assert_close, build_fp16, golden_arrays, golden_meta, torch_reference
 
 pytestmark = pytest.mark.gpu
 
@@ -199,26 +199,6 @@ def test_head_dims_groups_and_page_sizes(D, Hq, Hkv, bs):
     for ns in (1, 3, None):
         out = paged_decode_attention(*_to_gpu(c), num_splits=ns)
         assert_close(out.cpu().numpy(), ref, what=f"D={D} Hq={Hq} Hkv={Hkv} bs={bs} ns={ns}")
-
-
-def torch_reference(q, k_cache, v_cache, block_table, seq_lens, scale=None):
-    """fp32 torch restatement of reference.py:20-49 on the GPU (large cases only)."""
-    B, Hq, D = q.shape
-    _, bs, Hkv, _ = k_cache.shape
-    group = Hq // Hkv
-    scale = scale or D ** -0.5
-    out = torch.empty(B, Hq, D, dtype=torch.float32, device=q.device)
-    for b in range(B):
-        n = int(seq_lens[b])
-        nb = (n + bs - 1) // bs
-        blocks = block_table[b, :nb].long()
-        k = k_cache[blocks].reshape(-1, Hkv, D)[:n].float()
-        v = v_cache[blocks].reshape(-1, Hkv, D)[:n].float()
-        qb = q[b].float().reshape(Hkv, group, D)
-        s = torch.einsum("hgd,nhd->hgn", qb, k) * scale
-        p = torch.softmax(s, dim=-1)
-        out[b] = torch.einsum("hgn,nhd->hgd", p, v).reshape(Hq, D)
-    return out
 
 
 @pytest.mark.parametrize("B,ctx", [(8, 16384), (1, 65536)])

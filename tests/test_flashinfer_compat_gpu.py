@@ -55,7 +55,7 @@ def test_matches_flashinfer(layout, Hq, Hkv, D, ps):
     assert torch.equal(got, got_t) and (got2.float() - got.float()).abs().max().item() < 1e-3
     assert (lse2 - want_lse).abs().max().item() < 1e-3, "log-sum-exp (base 2) differs"
     # and both against fp32 attention computed directly from the pages
-    from test_decode_gpu import torch_reference
+    from helpers import torch_reference
     k = kv[:, 0] if layout == "NHD" else kv[:, 0].transpose(1, 2)
     v = kv[:, 1] if layout == "NHD" else kv[:, 1].transpose(1, 2)
     ref = torch_reference(q, k, v, ours._bt, ours._sl)

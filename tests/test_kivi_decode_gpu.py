@@ -126,7 +126,7 @@ def test_full_size_quantized_batch(fmt, B):
     attention on the dequantized cache."""
     from bpt.cache import ragged_lengths
     from bpt.quant import empty_kivi_cache, paged_decode_attention_kivi, quantize_append
-    from test_decode_gpu import torch_reference
+    from helpers import torch_reference
     ctx, bs, Hq, Hkv, D = 32768, 64, 32, 8, 128
     lens = ragged_lengths(B, ctx, seed=3)
     g = torch.Generator(device="cuda").manual_seed(5)
