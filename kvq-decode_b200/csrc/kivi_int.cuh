@@ -8,9 +8,10 @@
 // integer accumulation is exact. The fp operands become fixed point instead:
 //
 //   QK^T   q'_d = q_d * k_scale_d (per page, q head, channel) -> x = round(q' * 2^Ek),
-//          |x| < 2^22, split into three balanced signed bytes (x = l0 + 256 l1 + 65536 l2).
-//          MMA rows: 0-3 = limb 0 of heads 0-3, 8-11 = limb 1, 4-7 = limb 2, 12-15 = 0.
-//          S = (L0 + 256 L1 + 65536 L2) * 2^-Ek + sum_d q_d k_zero_d          (fp32 after)
+//          |x| < 2^30, split into four balanced signed bytes (x = sum_k l_k 256^k). Every
+//          token of a page shares the rounding of x, so x keeps all the bits the limbs hold.
+//          MMA rows: 0-3 = limb 0 of heads 0-3, 8-11 = limb 1, 4-7 = limb 2, 12-15 = limb 3.
+//          S = (L0 + 256 L1 + 65536 (L2 + 256 L3)) * 2^-Ek + sum_d q_d k_zero_d  (fp32 after)
 //   P.V    p'_t = p_t * v_scale_t -> round(p' * 2^Ev) < 2^32, four unsigned bytes. MMA_a
 //          columns = limb 0 | limb 1 (heads 0-3 each), MMA_b = limb 2 | limb 3; A = value
 //          codes transposed to (channel rows, 4 tokens per register).
@@ -47,7 +48,7 @@ struct ICfg {
   // nslot = CHUNK / box_rows is a launch-time value (1 for block_size >= CHUNK)
   static constexpr int STAGE_FIXED = K_BYTES + V_BYTES + VP_BYTES;
   static constexpr int FQ_ROW = 144;                       // 128 B of limbs + bank padding
-  static constexpr int FQ_SLOT = 12 * FQ_ROW;              // rows 12-15 are zero: not stored
+  static constexpr int FQ_SLOT = 16 * FQ_ROW;              // 16 limb rows
   static constexpr size_t MERGE_BYTES = size_t(NW) * 8 * (D + 2) * 4;
   __host__ __device__ static constexpr int stage_bytes(int nslot) {
     return (STAGE_FIXED + nslot * 512 + 1023) & ~1023;
@@ -57,7 +58,7 @@ struct ICfg {
                ? size_t(STAGES) * stage_bytes(nslot)
                : MERGE_BYTES;
   }
-  // q limbs [buf 2][slot][row 12][FQ_ROW], then {bias', kdown'} [buf 2][slot][head 4]
+  // q limbs [buf 2][slot][row 16][FQ_ROW], then {bias', kdown'} [buf 2][slot][head 4]
   __host__ __device__ static constexpr size_t fq_bytes(int nslot) {
     return size_t(2) * nslot * (FQ_SLOT + 32);
   }
@@ -345,14 +346,14 @@ kivi_int_decode_kernel(const __grid_constant__ CUtensorMap tmK,
         const uint32_t qm = redux_max_u32(__float_as_uint(lm));
 #pragma unroll
         for (int off = 16; off >= 1; off >>= 1) bsum += __shfl_xor_sync(kFullMask, bsum, off);
-        // |q' 2^ek| < 2^22 keeps the top balanced limb inside int8
-        const int ek = qm ? min(126, 21 - exponent_of_bits(qm)) : 0;
+        // |q' 2^ek| < 2^30 keeps the top of four balanced limbs inside int8
+        const int ek = qm ? min(126, 29 - exponent_of_bits(qm)) : 0;
         const float kup = exp2i(ek);
-        const uint32_t y0 = uint32_t(__float2int_rn(qs0 * kup) + 0x808080);
-        const uint32_t y1 = uint32_t(__float2int_rn(qs1 * kup) + 0x808080);
-        const uint32_t y2 = uint32_t(__float2int_rn(qs2 * kup) + 0x808080);
-        const uint32_t y3 = uint32_t(__float2int_rn(qs3 * kup) + 0x808080);
-        // x + 0x808080 = sum_k (l_k + 128) 256^k: byte k ^ 0x80 is the signed limb l_k
+        const uint32_t y0 = uint32_t(__float2int_rn(qs0 * kup)) + 0x80808080u;
+        const uint32_t y1 = uint32_t(__float2int_rn(qs1 * kup)) + 0x80808080u;
+        const uint32_t y2 = uint32_t(__float2int_rn(qs2 * kup)) + 0x80808080u;
+        const uint32_t y3 = uint32_t(__float2int_rn(qs3 * kup)) + 0x80808080u;
+        // x + 0x80808080 = sum_k (l_k + 128) 256^k: byte k ^ 0x80 is the signed limb l_k
         uint8_t* slot = fq + j * C::FQ_SLOT + 4 * lane;
         *reinterpret_cast<uint32_t*>(slot + warp * C::FQ_ROW) =
             byte_sel(y0, y1, y2, y3, 0u) ^ 0x80808080u;
@@ -360,6 +361,8 @@ kivi_int_decode_kernel(const __grid_constant__ CUtensorMap tmK,
             byte_sel(y0, y1, y2, y3, 1u) ^ 0x80808080u;
         *reinterpret_cast<uint32_t*>(slot + (4 + warp) * C::FQ_ROW) =
             byte_sel(y0, y1, y2, y3, 2u) ^ 0x80808080u;
+        *reinterpret_cast<uint32_t*>(slot + (12 + warp) * C::FQ_ROW) =
+            byte_sel(y0, y1, y2, y3, 3u) ^ 0x80808080u;
         if (lane == 0)
           *reinterpret_cast<float2*>(qp + j * 8 + warp * 2) =
               make_float2(bsum * p.scale_log2, exp2i(-ek) * p.scale_log2);
@@ -378,7 +381,7 @@ kivi_int_decode_kernel(const __grid_constant__ CUtensorMap tmK,
     }
 
     // ---- S = q'_int . codes: lanes g < 4 hold limbs 0 (rows g) and 1 (rows g + 8),
-    //      lanes g >= 4 limb 2 (rows g); own = their share of head (g & 3)
+    //      lanes g >= 4 limbs 2 (rows g) and 3 (rows g + 8); own = their share of head g & 3
     float own[4][2];
     uint32_t A[8], Bq[8];
 #pragma unroll
@@ -389,14 +392,10 @@ kivi_int_decode_kernel(const __grid_constant__ CUtensorMap tmK,
         const uint4 ra1 = *reinterpret_cast<const uint4*>(fr + g * C::FQ_ROW + 16);
         A[0] = ra0.x; A[1] = ra0.y; A[2] = ra0.z; A[3] = ra0.w;
         A[4] = ra1.x; A[5] = ra1.y; A[6] = ra1.z; A[7] = ra1.w;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) Bq[i] = 0u;
-        if (!upper) {
-          const uint4 rb0 = *reinterpret_cast<const uint4*>(fr + (g + 8) * C::FQ_ROW);
-          const uint4 rb1 = *reinterpret_cast<const uint4*>(fr + (g + 8) * C::FQ_ROW + 16);
-          Bq[0] = rb0.x; Bq[1] = rb0.y; Bq[2] = rb0.z; Bq[3] = rb0.w;
-          Bq[4] = rb1.x; Bq[5] = rb1.y; Bq[6] = rb1.z; Bq[7] = rb1.w;
-        }
+        const uint4 rb0 = *reinterpret_cast<const uint4*>(fr + (g + 8) * C::FQ_ROW);
+        const uint4 rb1 = *reinterpret_cast<const uint4*>(fr + (g + 8) * C::FQ_ROW + 16);
+        Bq[0] = rb0.x; Bq[1] = rb0.y; Bq[2] = rb0.z; Bq[3] = rb0.w;
+        Bq[4] = rb1.x; Bq[5] = rb1.y; Bq[6] = rb1.z; Bq[7] = rb1.w;
       }
 #pragma unroll
       for (int nbi = 0; nbi < 2; ++nbi) {
@@ -423,9 +422,9 @@ kivi_int_decode_kernel(const __grid_constant__ CUtensorMap tmK,
             mma_s8u8(sacc, A[2 * ks], Bq[2 * ks], A[2 * ks + 1], Bq[2 * ks + 1], w[2 * ks],
                      w[2 * ks + 1]);
         }
-        // rows g + 8 of upper lanes are zero, so one formula serves both halves
-        own[nb][0] = fmaf(256.f, float(sacc[2]), mA * float(sacc[0]));
-        own[nb][1] = fmaf(256.f, float(sacc[3]), mA * float(sacc[1]));
+        // lower lanes: L0 + 256 L1; upper lanes: 65536 (L2 + 256 L3)
+        own[nb][0] = mA * fmaf(256.f, float(sacc[2]), float(sacc[0]));
+        own[nb][1] = mA * fmaf(256.f, float(sacc[3]), float(sacc[1]));
       }
     }
 
@@ -507,9 +506,13 @@ kivi_int_decode_kernel(const __grid_constant__ CUtensorMap tmK,
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const float pe = fast_exp2(x[k] - m_use);
-      l_run += pe;
-      z_run = fmaf(pe, vz[k], z_run);
-      pm[k] = __float2uint_rn(pe * (vs[k] * vup));   // saturates at 2^32 - 1
+      const float vsup = vs[k] * vup;
+      pm[k] = __float2uint_rn(pe * vsup);   // saturates at 2^32 - 1
+      // l and z take the weight the token enters the MMA with, p' / (v_scale 2^vexp), so a
+      // token whose p' rounds to 0 drops out whole instead of leaving its v_zero behind
+      const float pw = vsup > 0.f ? float(pm[k]) * __frcp_rn(vsup) : pe;
+      l_run += pw;
+      z_run = fmaf(pw, vz[k], z_run);
     }
 #pragma unroll
     for (int k = 0; k < 4; ++k) po[k] = __shfl_xor_sync(kFullMask, pm[k], 16);

@@ -7,24 +7,30 @@
 //   QK^T   D_qk[token][16 j + 4 h + limb] = sum_k K[token][k] * B_qk[16 j + 4 h + limb][k]
 //          M = 128 tokens, N = 16 per page slot j, K = 128 channel bytes (4 MMAs of 32).
 //          A = the key code tile exactly as TMA stored it (K-major, 128-byte swizzle). B = the
-//          q' limbs: x = round(q * k_scale * 2^Ek) (|x| < 2^22) as three balanced signed
+//          q' limbs: x = round(q * k_scale * 2^Ek) (|x| < 2^30) as four balanced signed
 //          bytes, written by the warps in the same K-major swizzled layout.
 //          INT4: a packed byte is lo + 16 hi (lo = even channel), so
-//            sum_k lo_k x_2k + hi_k x_2k+1 = sum_k byte_k v_k + lo_k (x_2k - v_k),
-//          v_k = round(x_2k+1 / 16) (the odd channels' x taken as 16 v_k; INT4 x uses four
-//          limbs, |x| < 2^26, so v keeps 22 bits). Two MMAs read the
-//          packed tile as TMA stored it (64-byte rows, 64-byte swizzle) against B rows of v,
-//          two read a low-nibble copy (one AND per word, same layout) against rows of x_2k - v.
-//          S_h = (L0 + 256 L1 + 65536 L2 [+ 2^24 L3, INT4]) * 2^-Ek + sum_d q_d k_zero_d
+//            16 sum_k (lo_k x_2k + hi_k x_2k+1) = sum_k byte_k x_2k+1 + lo_k (16 x_2k - x_2k+1)
+//          (|x| < 2^26, so 16 x_2k - x_2k+1 fits four limbs). Two MMAs read the packed tile as
+//          TMA stored it (64-byte rows, 64-byte swizzle) against B rows of x_2k+1, two read a
+//          low-nibble copy (one AND per word, same layout) against rows of 16 x_2k - x_2k+1.
+//          S_h = (L0 + 256 L1 + 65536 L2 + 2^24 L3) * 2^-Ek [/ 16, INT4] + sum_d q_d k_zero_d
 //   P.V    D_pv[channel][4 h + limb] += sum_t V[t][channel] * P'[t][4 h + limb]
 //          M = 128 channels, N = 16, K = 128 tokens. A = the value code tile read MN-major
 //          (token rows of 128 channel bytes, as TMA stored it), B = P' rows of 16 bytes: the
 //          four little-endian bytes of p'_h = round(p_h * v_scale_t * 2^Ev) < 2^32.
-//          INT4: value bytes pack tokens 2p (lo) and 2p + 1 (hi); as for the keys, two MMAs
-//          read the packed pair rows against rows of v_p = round(p'_2p+1 / 16) and two read a
-//          low-nibble copy against rows of p'_2p - v_p, both as balanced signed bytes
-//          (p' < 2^30).
-//          O_h = D_pv combined over limbs * 2^-Ev + sum_t p_h v_zero_t          (fp32)
+//          INT4: value bytes pack tokens 2p (lo) and 2p + 1 (hi). The compute warps split the
+//          tile into a low-nibble copy (even tokens) and a high-nibble copy (odd tokens), same
+//          layout; two MMAs read each against the P' rows of its tokens, so every token's p'
+//          keeps all 32 bits (a packed-byte form would round the odd tokens' p' to multiples
+//          of 16, and in very peaked softmaxes the many small weights near that step are lost).
+//          O_h = D_pv combined over limbs * 2^-Ev + sum_t p~_h v_zero_t          (fp32)
+//          The normaliser and the zero-point sum use the weight each token actually entered
+//          the MMA with, p~ = p' / (v_scale_t 2^Ev) (p itself for a token whose v_scale is 0).
+//          With the exact p there, a token whose p' rounds to 0 would still add its v_zero
+//          (the minimum of its values) while its v_scale * code part is dropped: a bias that
+//          grows with the tokens of a split and that the cancellation between the two sums
+//          amplifies wherever the output is small.
 //
 // Thread t owns token t for the softmax (no redundancy: its 4 heads are 4 registers) and
 // channel t when D_pv is read back. The softmax reference m_ref (per head) and the value
@@ -39,7 +45,7 @@
 // committed (tcgen05.commit on the slot's "empty" barrier). Per chunk c the compute warps read
 // S(c) from TMEM, quantize q for chunk c + 1 (INT4: and copy its keys' low nibbles) and
 // publish it (QK(c + 1) overlaps the rest of the chunk), exchange chunk maxima, then
-// (PV(c - 1) done) write P'(c) (INT4: and chunk c's value low nibbles) for PV(c). INT4 calls
+// (PV(c - 1) done) write P'(c) (INT4: and chunk c's value nibble tiles) for PV(c). INT4 calls
 // at large batch and long context use a 2-slot value ring (3 CTAs per SM). Every wait on
 // TMA / MMA completion or on another warp is time-bounded; a failed wait raises a shared
 // abort flag.
@@ -132,6 +138,7 @@ struct TCfg {
   static constexpr int VS_BYTES = CHUNK * 16;               // v_scale [token][8 heads] fp16
   static constexpr int KX_BYTES = INT4 ? CHUNK * 64 : 0;        // low nibbles of the keys
   static constexpr int VX_BYTES = INT4 ? CHUNK / 2 * 128 : 0;   // low nibbles of the values
+  static constexpr int VH_BYTES = VX_BYTES;                     // high nibbles of the values
   static constexpr int P_BYTES = CHUNK * 16;                // P' [token][16 B]
   // K slot = key tile + the chunk's k_scale | k_zero rows (nslot x 512 B); V slot = value
   // tile + v_scale and v_zero of the chunk's tokens for the 8 heads around this one
@@ -149,7 +156,7 @@ struct TCfg {
   }
   __host__ __device__ static constexpr size_t smem_bytes(int nslot) {
     return 1024 + size_t(SK) * kslot_bytes(nslot) + size_t(SV) * vslot_bytes() + KX_BYTES +
-           VX_BYTES + bqk_bytes(nslot) + P_BYTES + misc_bytes(nslot);
+           VX_BYTES + VH_BYTES + bqk_bytes(nslot) + P_BYTES + misc_bytes(nslot);
   }
   // TMEM: D_qk at columns [0, 16 nslot), D_pv (16 columns) at pv_col
   __host__ __device__ static constexpr uint32_t pv_col(int nslot) {
@@ -195,9 +202,10 @@ kivi_tc_decode_kernel(const __grid_constant__ CUtensorMap tmK,
   uint8_t* vring = kring + SK * kslot;
   uint8_t* kx = vring + SV * vslot;                        // INT4 low-nibble key tile
   uint8_t* vx = kx + C::KX_BYTES;                          // INT4 low-nibble value tile
+  uint8_t* vh = vx + C::VX_BYTES;                          // INT4 high-nibble value tile
   // q' limb rows (K-major; INT8 128-byte rows, 128-byte swizzle; INT4 two sets of 64-byte
   // rows, 64-byte swizzle: v rows for the packed tile, then x - v rows for the low nibbles)
-  uint8_t* bqk = vx + C::VX_BYTES;
+  uint8_t* bqk = vh + C::VH_BYTES;
   // P' [token][16 B] (INT4: [pair][16 B] of v for the packed tile, then of p' - v)
   uint8_t* pbuf = bqk + C::bqk_bytes(nslot);
   uint8_t* misc = pbuf + C::P_BYTES;
@@ -390,7 +398,7 @@ kivi_tc_decode_kernel(const __grid_constant__ CUtensorMap tmK,
     // ================================================================ MMA warp (lane 0)
     if (lane == 0) {
       const uint32_t id_qk = tc::idesc_i8(128, 16 * nslot, false, true, false, false);
-      const uint32_t id_pv = tc::idesc_i8(128, 16, false, INT4, true, true);
+      const uint32_t id_pv = tc::idesc_i8(128, 16, false, false, true, true);
       auto issue_pv = [&](int cc) {
         if (!mbar_wait(pready, uint32_t(cc) & 1u)) {
           *abort_flag = 1;
@@ -401,8 +409,10 @@ kivi_tc_decode_kernel(const __grid_constant__ CUtensorMap tmK,
         const uint32_t acc0 = *pv_reset ? 0u : 1u;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          // INT4: k = 0, 1 the packed pair rows, k = 2, 3 their low nibbles (32 rows each)
-          const uint32_t a = INT4 ? (k < 2 ? a0 : smem_u32(vx)) + 4096 * (k & 1) : a0 + 4096 * k;
+          // INT4: k = 0, 1 the high nibbles (odd tokens), k = 2, 3 the low nibbles (even
+          // tokens), 32 pair rows each, against the P' rows of those tokens
+          const uint32_t a = INT4 ? (k < 2 ? smem_u32(vh) : smem_u32(vx)) + 4096 * (k & 1)
+                                  : a0 + 4096 * k;
           tc::mma_i8(tmem + pv_col, tc::smem_desc(a, 16384, 1024, tc::kSw128),
                      tc::smem_desc(b0 + 512 * k, 128, 256, tc::kSwNone), id_pv,
                      k == 0 ? acc0 : 1u);
@@ -498,44 +508,44 @@ kivi_tc_decode_kernel(const __grid_constant__ CUtensorMap tmK,
       const uint32_t bm = redux_max_nv(__float_as_uint(fabsf(bp)));
       const int eb = bm ? min(126, 24 - exponent_of_bits(bm)) : 0;
       const float bsum = float(redux_add_s32(__float2int_rn(bp * exp2i(eb)))) * exp2i(-eb);
-      // |q' 2^ek| < 2^22 keeps the top of three balanced limbs inside int8. INT4 uses four
-      // limbs and |q' 2^ek| < 2^26, so the odd channels' v = round(x / 16) keeps 22 bits.
-      const int ek = qm ? min(126, (INT4 ? 25 : 21) - exponent_of_bits(qm)) : 0;
+      // Four balanced limbs. INT8: |q' 2^ek| < 2^30 (a product of two fp16 values has 22
+      // significant bits, so the largest channels' x is exact). Every token of a page shares
+      // the rounding of x, weighted by its codes (about half their range on average), so x
+      // carries all the bits the limbs hold: a coarser x shifts whole pages' scores together.
+      // INT4: |q' 2^ek| < 2^26, so b = 16 x_even - x_odd below fits the four limbs.
+      const int ek = qm ? min(122, (INT4 ? 25 : 29) - exponent_of_bits(qm)) : 0;
       const float kup = exp2i(ek);
       int x0 = __float2int_rn(qs0 * kup), x1 = __float2int_rn(qs1 * kup);
       int x2 = __float2int_rn(qs2 * kup), x3 = __float2int_rn(qs3 * kup);
       if constexpr (INT4) {
-        // lanes 16-31 (odd channels): v = round(x / 16), for the packed tile; lanes 0-15 (even
-        // channels of the same pairs): x - v of the partner lane, for the low-nibble tile
-        const float kq = kup * 0.0625f;
-        const int v0 = __float2int_rn(qs0 * kq), v1 = __float2int_rn(qs1 * kq);
-        const int v2 = __float2int_rn(qs2 * kq), v3 = __float2int_rn(qs3 * kq);
-        const int w0 = __shfl_xor_sync(kFullMask, v0, 16), w1 = __shfl_xor_sync(kFullMask, v1, 16);
-        const int w2 = __shfl_xor_sync(kFullMask, v2, 16), w3 = __shfl_xor_sync(kFullMask, v3, 16);
+        // A packed byte is lo + 16 hi (lo = even channel). The packed tile meets a = x_odd
+        // (lanes 16-31) and the low-nibble copy meets b = 16 x_even - x_odd (lanes 0-15, the
+        // partner lane holds x_odd of the same pairs): sum byte a + lo b = 16 sum (lo x_even
+        // + hi x_odd), every channel at full precision; kdown carries the 2^-4.
+        const int w0 = __shfl_xor_sync(kFullMask, x0, 16), w1 = __shfl_xor_sync(kFullMask, x1, 16);
+        const int w2 = __shfl_xor_sync(kFullMask, x2, 16), w3 = __shfl_xor_sync(kFullMask, x3, 16);
         const bool lo_lane = lane < 16;
-        x0 = lo_lane ? x0 - w0 : v0;
-        x1 = lo_lane ? x1 - w1 : v1;
-        x2 = lo_lane ? x2 - w2 : v2;
-        x3 = lo_lane ? x3 - w3 : v3;
+        x0 = lo_lane ? 16 * x0 - w0 : x0;
+        x1 = lo_lane ? 16 * x1 - w1 : x1;
+        x2 = lo_lane ? 16 * x2 - w2 : x2;
+        x3 = lo_lane ? 16 * x3 - w3 : x3;
       }
-      // x + 0x80808080 (INT4, four limbs) or x + 0x808080 (three limbs) = sum_k (l_k + 128)
-      // 256^k: byte k ^ 0x80 is the signed limb l_k
-      constexpr uint32_t kBias = INT4 ? 0x80808080u : 0x808080u;
+      // x + 0x80808080 = sum_k (l_k + 128) 256^k: byte k ^ 0x80 is the signed limb l_k
+      constexpr uint32_t kBias = 0x80808080u;
       const uint32_t y0 = uint32_t(x0) + kBias, y1 = uint32_t(x1) + kBias;
       const uint32_t y2 = uint32_t(x2) + kBias, y3 = uint32_t(x3) + kBias;
-      // x + 0x808080 = sum_k (l_k + 128) 256^k: byte k ^ 0x80 is the signed limb l_k
       return Limbs{byte_sel(y0, y1, y2, y3, 0u) ^ 0x80808080u,
                    byte_sel(y0, y1, y2, y3, 1u) ^ 0x80808080u,
                    byte_sel(y0, y1, y2, y3, 2u) ^ 0x80808080u,
-                   INT4 ? byte_sel(y0, y1, y2, y3, 3u) ^ 0x80808080u : 0u, bsum * p.scale_log2,
-                   exp2i(-ek) * p.scale_log2};
+                   byte_sel(y0, y1, y2, y3, 3u) ^ 0x80808080u, bsum * p.scale_log2,
+                   exp2i(-ek - (INT4 ? 4 : 0)) * p.scale_log2};
     };
     auto store_limbs = [&](int j, int cc, const Limbs& L) {
       const int row0 = 16 * j + 4 * warp;
       const uint32_t cofs = (uint32_t(lane) & 3u) << 2;
       const uint32_t lv[4] = {L.l0, L.l1, L.l2, L.l3};
 #pragma unroll
-      for (int limb = 0; limb < (INT4 ? 4 : 3); ++limb) {
+      for (int limb = 0; limb < 4; ++limb) {
         const int row = row0 + limb;
         if constexpr (INT4) {   // pair bytes 4 (lane & 15) .. + 3 of a 64-byte swizzled row
           uint8_t* set = bqk + (lane < 16 ? nslot * 16 * 64 : 0);
@@ -559,6 +569,21 @@ kivi_tc_decode_kernel(const __grid_constant__ CUtensorMap tmK,
           const uint4 w = *reinterpret_cast<const uint4*>(src + o);
           *reinterpret_cast<uint4*>(dst + o) = make_uint4(
               w.x & 0x0F0F0F0Fu, w.y & 0x0F0F0F0Fu, w.z & 0x0F0F0F0Fu, w.w & 0x0F0F0F0Fu);
+        }
+      }
+    };
+    // low and high nibbles of a packed INT4 value tile into two tiles of the same layout
+    auto split_nibbles = [&](const uint8_t* src, uint8_t* lo, uint8_t* hi, int bytes) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int o = 16 * (tid + i * C::CONSUMERS);
+        if (o < bytes) {
+          const uint4 w = *reinterpret_cast<const uint4*>(src + o);
+          *reinterpret_cast<uint4*>(lo + o) = make_uint4(
+              w.x & 0x0F0F0F0Fu, w.y & 0x0F0F0F0Fu, w.z & 0x0F0F0F0Fu, w.w & 0x0F0F0F0Fu);
+          *reinterpret_cast<uint4*>(hi + o) =
+              make_uint4((w.x >> 4) & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu,
+                         (w.z >> 4) & 0x0F0F0F0Fu, (w.w >> 4) & 0x0F0F0F0Fu);
         }
       }
     };
@@ -635,7 +660,7 @@ kivi_tc_decode_kernel(const __grid_constant__ CUtensorMap tmK,
         for (int hh = 0; hh < 4; ++hh) {
           float s = fmaf(65536.f, float(int(r[4 * hh + 2])),
                          fmaf(256.f, float(int(r[4 * hh + 1])), float(int(r[4 * hh]))));
-          if constexpr (INT4) s = fmaf(16777216.f, float(int(r[4 * hh + 3])), s);
+          s = fmaf(16777216.f, float(int(r[4 * hh + 3])), s);
           const float2 q2 = qpb[hh];
           x[hh] = valid ? fmaf(s, q2.y, q2.x) : kNegInf;
         }
@@ -668,9 +693,9 @@ kivi_tc_decode_kernel(const __grid_constant__ CUtensorMap tmK,
       const uint32_t vmb = xc[4];
       if (tid < 8) xchg[((c + 2) % 3) * 8 + tid] = tid < 4 ? tc::kOrdNegInf : 0u;
 
-      // ---- PV of chunk c - 1 done: P' / the values' low-nibble tile are free, D_pv is final
+      // ---- PV of chunk c - 1 done: P' / the values' nibble tiles are free, D_pv is final
       if (c >= 1) wait_or_abort(pv_bar, c - 1);
-      if constexpr (INT4) low_nibbles(vb, vx, C::VX_BYTES);
+      if constexpr (INT4) split_nibbles(vb, vx, vh, C::VX_BYTES);
 
       // ---- reference max / value exponent (uniform over the CTA); read D_pv back if needed
       bool need[4], m_rebase = false;
@@ -685,8 +710,7 @@ kivi_tc_decode_kernel(const __grid_constant__ CUtensorMap tmK,
         const int ve = 31 - int(kSoftmaxHeadroom) - exponent_of_bits(vmb);
         if (vexp == kExpUnset || ve < vexp) {
           v_rebase = vexp != kExpUnset;
-          // INT4: one more bit, so p' - v stays inside four balanced signed bytes
-          vexp_new = max(-126, min(126, ve - kValueHeadroom - (INT4 ? 1 : 0)));
+          vexp_new = max(-126, min(126, ve - kValueHeadroom));
         }
       }
       if (since_flush > 0 && (m_rebase || v_rebase || since_flush >= 256) && !*cabort) {
@@ -707,25 +731,19 @@ kivi_tc_decode_kernel(const __grid_constant__ CUtensorMap tmK,
         }
       }
       const float vsup = vs * exp2i(vexp == kExpUnset ? 0 : vexp);
+      // 1 / (v_scale 2^Ev): turns a token's p' back into the weight the MMA gives it
+      const float vinv = vsup > 0.f ? __frcp_rn(vsup) : 0.f;
       uint32_t pq[4];
 #pragma unroll
       for (int hh = 0; hh < 4; ++hh) {
         const float pe = fast_exp2(x[hh] - (m_ref[hh] == kNegInf ? 0.f : m_ref[hh]));
-        l_run[hh] += pe;
-        z_run[hh] = fmaf(pe, vz, z_run[hh]);
-        if constexpr (INT4) {
-          // pair p = tokens 2p (thread 2p) and 2p + 1: the odd token's v = round(p' / 16) goes
-          // to the packed tile's row p, the even token's p' - v to the low-nibble tile's row p,
-          // both as balanced signed bytes (x + 0x80808080: byte ^ 0x80 is the signed limb)
-          const float pv = pe * vsup;
-          const int v = __float2int_rn(pv * 0.0625f);
-          const int w = __shfl_xor_sync(kFullMask, v, 1);
-          const int x = (tid & 1) ? v : __float2int_rn(pv) - w;
-          pq[hh] = (uint32_t(x) + 0x80808080u) ^ 0x80808080u;
-        } else {
-          pq[hh] = __float2uint_rn(pe * vsup);   // saturates at 2^32 - 1
-        }
+        pq[hh] = __float2uint_rn(pe * vsup);   // saturates at 2^32 - 1
+        // the token's weight as the MMA sees it, so l and z stay consistent with D_pv
+        const float pw = vsup > 0.f ? float(pq[hh]) * vinv : pe;
+        l_run[hh] += pw;
+        z_run[hh] = fmaf(pw, vz, z_run[hh]);
       }
+      // INT4: odd tokens' P' rows first (they meet the high-nibble tile), then even tokens'
       uint8_t* prow = INT4 ? pbuf + ((tid & 1) ? 0 : 1024) + 16 * (tid >> 1) : pbuf + 16 * tid;
       *reinterpret_cast<uint4*>(prow) = make_uint4(pq[0], pq[1], pq[2], pq[3]);
       if (tid == 0) *pv_reset = reset_pv ? 1 : 0;
