@@ -749,7 +749,25 @@ def run_sweep(args, dev, sms, checker, peak, local):
     if "fp16_b1_ctx128k" in out and "int4_b1_ctx128k" in out:
         res["int4_vs_fp16_latency_128k"] = (out["fp16_b1_ctx128k"]["us_per_layer"]
                                             / out["int4_b1_ctx128k"]["us_per_layer"])
+    res["accuracy"] = run_accuracy(args, dev)
     return res
+
+
+def run_accuracy(args, dev, ctx=131072):
+    """The KIVI formats' accuracy at 128k tokens through the decode kernels (bpt.accuracy):
+    needle weight recovered per q head, and output error against the fp16 cache."""
+    import torch
+    from bpt.accuracy import needle_inputs, needle_study, summarize
+    inputs = needle_inputs(ctx, seed=args.seed, device=dev)
+    out = {"method": "needle in a BASELINE-distribution haystack (4 x10 outlier key channels "
+                     "per kv head), one sequence of 131072 tokens, block_size 64; weights "
+                     "measured through the kernels (two decodes differing only in the needle's "
+                     "value); output error of each format against bpt's fp16 decode"}
+    for fmt in ("int8", "fp8", "int4"):
+        out[fmt] = summarize(needle_study(fmt, ctx, inputs=inputs))
+    del inputs
+    torch.cuda.empty_cache()
+    return out
 
 
 def torch_partial_state(q_b, k, v):
