@@ -1073,9 +1073,15 @@ def run_bpt(args):
         if world == 1:
             sweep = run_sweep(args, dev, sms, checker, peak, local)
         elif not seqshard:
-            seqshard_suite = {f"{n}_{x}": run_seqshard_point(n, x, args, world, rank, local,
-                                                             dev, sms)
-                              for n, x in SEQSHARD}
+            seqshard_suite = {}
+            for n, x in SEQSHARD:
+                try:
+                    seqshard_suite[f"{n}_{x}"] = run_seqshard_point(n, x, args, world, rank,
+                                                                    local, dev, sms)
+                except Exception as e:  # noqa: BLE001 - recorded in the line, headline kept
+                    seqshard_suite[f"{n}_{x}"] = {"error": f"{type(e).__name__}: {e}"[:300]}
+                    torch.cuda.synchronize()
+                    torch.cuda.empty_cache()
 
     if world > 1:
         torch.cuda.synchronize()
@@ -1143,7 +1149,8 @@ def run_bpt(args):
         line["seqshard"] = seqshard_suite
     print(json.dumps(line), flush=True)
     oks = [parity] + ([p["parity"] for p in sweep["points"].values()] if sweep else []) + \
-          ([p["parity"] for p in seqshard_suite.values()] if seqshard_suite else [])
+          ([p["parity"] for p in seqshard_suite.values() if "parity" in p]
+           if seqshard_suite else [])
     if any(p is not None and not p["ok"] for p in oks):
         print("bench: parity check failed (see the parity keys of the JSON line)",
               file=sys.stderr)
