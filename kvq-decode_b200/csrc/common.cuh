@@ -128,6 +128,26 @@ __device__ __forceinline__ void pdl_wait() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
+// Launch `kern` as a programmatic dependent of the previous kernel in `st`: its CTAs may be
+// scheduled once that kernel's CTAs have all called pdl_launch_dependents() (or exited), and
+// they wait in pdl_wait() for its completion. After a kernel that never calls
+// pdl_launch_dependents() this only saves the launch latency.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_dependent(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                    cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<Args&&>(args)...);
+}
+
 // ----------------------------------------------------------------------------- misc
 
 __device__ __forceinline__ void named_barrier_sync(int id, int threads) {

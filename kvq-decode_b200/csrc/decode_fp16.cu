@@ -119,6 +119,10 @@ split_kv_fp16_kernel(const __grid_constant__ CUtensorMap tmK,
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = p.splits;
 
+  // launched as a programmatic dependent of the previous kernel in the stream: nothing that
+  // kernel may write (q, the cache, the table, the lengths, the workspace) is read before
+  // it completed
+  pdl_wait();
   int n = __ldg(p.seq_lens + b);
   if (n < 0) {
     if (threadIdx.x == 0) flag_device_error(p.status, BPT_DEV_NEG_SEQ_LEN);
@@ -443,6 +447,9 @@ merge_splits_kernel(const float* __restrict__ o_part, const float* __restrict__ 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nd4 = (D + 3) >> 2;
   pdl_wait();
+  // the next kernel in the stream (the next call's split kernel) may start launching: its CTAs
+  // take the SM slots this merge leaves free and wait for its completion
+  pdl_launch_dependents();
 
   for (int c0 = 0; c0 < nd4; c0 += 32) {
     const int c = c0 + lane;
@@ -537,8 +544,10 @@ int launch_split(const CUtensorMap& tk, const CUtensorMap& tv, const DecodeParam
                            int(G::SMEM_BYTES)) != cudaSuccess)
     return BPT_ERR_LAUNCH;
   dim3 grid(p.splits, p.kv_heads, p.batch);
-  kern<<<grid, kThreads, G::SMEM_BYTES, st>>>(tk, tv, p);
-  return BPT_OK;
+  return launch_dependent(kern, grid, dim3(kThreads), G::SMEM_BYTES, st, tk, tv, p) ==
+                 cudaSuccess
+             ? BPT_OK
+             : BPT_ERR_LAUNCH;
 }
 
 template <int D>

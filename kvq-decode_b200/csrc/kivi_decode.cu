@@ -171,6 +171,10 @@ kivi_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = p.splits;
 
+  // launched as a programmatic dependent of the previous kernel in the stream: nothing that
+  // kernel may write (q, the cache, the table, the lengths, the workspace) is read before
+  // it completed
+  pdl_wait();
   int n = __ldg(p.seq_lens + b);
   if (n < 0) {
     if (threadIdx.x == 0) flag_device_error(p.status, BPT_DEV_NEG_SEQ_LEN);
@@ -695,8 +699,10 @@ int launch(const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tks,
                            int(C::SMEM_BYTES)) != cudaSuccess)
     return BPT_ERR_LAUNCH;
   dim3 grid(kp.d.splits, kp.d.kv_heads, kp.d.batch);
-  kern<<<grid, C::THREADS, C::SMEM_BYTES, st>>>(tk, tv, tks, tkz, kp);
-  return BPT_OK;
+  return launch_dependent(kern, grid, dim3(C::THREADS), C::SMEM_BYTES, st, tk, tv, tks, tkz,
+                          kp) == cudaSuccess
+             ? BPT_OK
+             : BPT_ERR_LAUNCH;
 }
 
 #include "kivi_int.cuh"
@@ -785,8 +791,10 @@ int launch_tc(const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& t
       cudaSuccess)
     return BPT_ERR_LAUNCH;
   dim3 grid(kp.d.splits, kp.d.kv_heads, kp.d.batch);
-  kern<<<grid, C::THREADS, smem, st>>>(tk, tv, tks, tkz, tvs, tvz, kp);
-  return BPT_OK;
+  return launch_dependent(kern, grid, dim3(C::THREADS), smem, st, tk, tv, tks, tkz, tvs, tvz,
+                          kp) == cudaSuccess
+             ? BPT_OK
+             : BPT_ERR_LAUNCH;
 }
 
 template <int FMT>
@@ -800,8 +808,10 @@ int launch_int(const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& 
       cudaSuccess)
     return BPT_ERR_LAUNCH;
   dim3 grid(kp.d.splits, kp.d.kv_heads, kp.d.batch);
-  kern<<<grid, C::THREADS, smem, st>>>(tk, tv, tks, tkz, kp);
-  return BPT_OK;
+  return launch_dependent(kern, grid, dim3(C::THREADS), smem, st, tk, tv, tks, tkz, kp) ==
+                 cudaSuccess
+             ? BPT_OK
+             : BPT_ERR_LAUNCH;
 }
 
 }  // namespace kivi

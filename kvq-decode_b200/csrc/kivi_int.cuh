@@ -137,6 +137,10 @@ kivi_int_decode_kernel(const __grid_constant__ CUtensorMap tmK,
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = p.splits;
 
+  // launched as a programmatic dependent of the previous kernel in the stream: nothing that
+  // kernel may write (q, the cache, the table, the lengths, the workspace) is read before
+  // it completed
+  pdl_wait();
   int n = __ldg(p.seq_lens + b);
   if (n < 0) {
     if (threadIdx.x == 0) flag_device_error(p.status, BPT_DEV_NEG_SEQ_LEN);

@@ -237,6 +237,10 @@ kivi_tc_decode_kernel(const __grid_constant__ CUtensorMap tmK,
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int S = p.splits;
 
+  // launched as a programmatic dependent of the previous kernel in the stream: nothing that
+  // kernel may write (q, the cache, the table, the lengths, the workspace) is read before
+  // it completed
+  pdl_wait();
   int n = __ldg(p.seq_lens + b);
   if (n < 0) {
     if (tid == 0) flag_device_error(p.status, BPT_DEV_NEG_SEQ_LEN);

@@ -135,6 +135,10 @@ split_kv_fp16_mma_kernel(const __grid_constant__ CUtensorMap tmK,
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = p.splits;
 
+  // launched as a programmatic dependent of the previous kernel in the stream: nothing that
+  // kernel may write (q, the cache, the table, the lengths, the workspace) is read before
+  // it completed
+  pdl_wait();
   int n = __ldg(p.seq_lens + b);
   if (n < 0) {
     if (threadIdx.x == 0) flag_device_error(p.status, BPT_DEV_NEG_SEQ_LEN);
@@ -432,8 +436,10 @@ int launch(const CUtensorMap& tk, const CUtensorMap& tv, const DecodeParams& p,
                            int(C::SMEM_BYTES)) != cudaSuccess)
     return BPT_ERR_LAUNCH;
   dim3 grid(p.splits, p.kv_heads, p.batch);
-  kern<<<grid, C::THREADS, C::SMEM_BYTES, st>>>(tk, tv, p);
-  return BPT_OK;
+  return launch_dependent(kern, grid, dim3(C::THREADS), C::SMEM_BYTES, st, tk, tv, p) ==
+                 cudaSuccess
+             ? BPT_OK
+             : BPT_ERR_LAUNCH;
 }
 
 }  // namespace mma

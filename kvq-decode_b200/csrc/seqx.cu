@@ -196,6 +196,9 @@ seq_exchange_kernel(const float* __restrict__ o_part, const float* __restrict__ 
     }
   }
 
+  // the next kernel in the stream may start launching; it waits for this grid's completion
+  pdl_launch_dependents();
+
   // ---- phase 2: every rank's state of my items -> the merged fp16 output. Thread d reads
   // every rank's lse word and o word d at once, then polls (time-bounded) only the words that
   // do not carry this call's epoch yet. Every word is awaited, even at weight 0, so no store
