@@ -223,8 +223,9 @@ int bpt_decode_fp16_noalloc(const void* q, int64_t q_sb, int64_t q_sh,
  * every rank. bufs[r] is rank r's buffer as mapped in this process (bufs[rank] = own). All
  * ranks must make the same sequence of calls with the same batch / q_heads / head_dim; a wait
  * that runs out sets BPT_DEV_WAIT_TIMEOUT in *status. head_dim % 4 == 0, <= 256; world <= 8.
- * The first bpt_seqx_merge_fp16 call on a device sizes the kernel's grid to what is resident
- * on that device (an occupancy query); make it before capturing the call in a CUDA graph. */
+ * A buffer serves one (world, batch, q_heads, head_dim). The first bpt_seqx_merge_fp16 call on
+ * a device sizes the kernel's grid to what is resident on that device (an occupancy query);
+ * make it before capturing the call in a CUDA graph. */
 #define BPT_IPC_HANDLE_BYTES 64
 size_t bpt_seqx_buffer_bytes(int world, int batch, int q_heads, int head_dim);
 int bpt_seqx_alloc(size_t bytes, void** buf, void* ipc_handle);

@@ -10,8 +10,8 @@
 //                                   o[0, D) then lse2,
 //                                   each value in its own word as {fp32 bits, epoch}; a slot is
 //                                   a whole number of 128-byte lines
-//   ctl    [32]                     ctl[0] (u32): epoch of the last finished call,
-//                                   ctl[1] (u32): CTAs done with the current call
+//   ctl    [B * Hq] (u32)           ctl[c]: epoch of the last call CTA c of the exchange
+//                                   kernel finished (the grid never exceeds B * Hq CTAs)
 //
 // Exchange protocol (the "low-latency" pattern of flag-carrying words): a value and the call's
 // epoch travel in ONE naturally aligned 8-byte store, which lands atomically, so a reader that
@@ -29,11 +29,14 @@
 //            o[d] -- all at once, polls (time-bounded) those that do not carry the epoch yet,
 //            and merges the world states into channel d of the fp16 output.
 // A CTA finishes all its phase-1 stores before it waits, and the grid never exceeds what is
-// resident at once, so no rank can wait on a CTA that cannot start. The epoch is
-// ctl[0] + 1; the last CTA to finish bumps ctl[0], so consecutive calls (also graph replays)
-// use fresh epochs and the buffer never needs clearing. A wait that runs out of its budget sets
-// BPT_DEV_WAIT_TIMEOUT in the status word and the kernel continues (the output is then wrong,
-// the GPU stays usable).
+// resident at once, so no rank can wait on a CTA that cannot start. Each CTA keeps its own
+// epoch: ctl[c] + 1, read together with its first split rows and written back when it is done,
+// so consecutive calls (also graph replays) use fresh epochs, the buffer never needs clearing,
+// and no CTA waits for another at the end. CTA c of every rank handles the same items and has
+// run in the same calls (the grid, min(B * Hq, resident CTAs), is the same on every rank and in
+// every call of one buffer), so writer and reader of a slot agree on its epoch. A wait that
+// runs out of its budget sets BPT_DEV_WAIT_TIMEOUT in the status word and the kernel continues
+// (the output is then wrong, the GPU stays usable).
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -105,11 +108,11 @@ seq_exchange_kernel(const float* __restrict__ o_part, const float* __restrict__ 
   const int nd4 = D >> 2;
   uint64_t* const* slots = reinterpret_cast<uint64_t* const*>(bufs.p);
   const size_t set_words = size_t(world) * items * slot_words(D);
-  unsigned* ctl = reinterpret_cast<unsigned*>(slots[rank] + 2 * set_words);
+  unsigned* ctl = reinterpret_cast<unsigned*>(slots[rank] + 2 * set_words) + blockIdx.x;
   pdl_wait();
-  const unsigned epoch = *reinterpret_cast<volatile unsigned*>(ctl) + 1u;
-  const size_t set0 = (epoch & 1u) * set_words;   // this call's slot set
-  uint64_t* mine = slots[rank] + set0;
+  // issued before the split rows' loads and first used after them: no extra round trip
+  unsigned epoch;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(epoch) : "l"(ctl) : "memory");
   int my_timeout = 0;
   if (tid == 0) timed_out = 0;
 
@@ -120,7 +123,6 @@ seq_exchange_kernel(const float* __restrict__ o_part, const float* __restrict__ 
   for (int it = blockIdx.x; it < items; it += gridDim.x) {
     const float* l = lse + int64_t(it) * splits;
     const float* o = o_part + int64_t(it) * splits * D;
-    const size_t base = set0 + (size_t(rank) * items + it) * slot_words(D);
     for (int c0 = 0; c0 < nd4; c0 += 32) {
       const int c = c0 + lane;
       const bool c_in = c < nd4;
@@ -183,14 +185,17 @@ seq_exchange_kernel(const float* __restrict__ o_part, const float* __restrict__ 
           }
         }
         const float inv = L > 0.f ? 1.f / L : 0.f;
+        const size_t base =
+            size_t((epoch + 1u) & 1u) * set_words + (size_t(rank) * items + it) * slot_words(D);
         if (c_in) {
           const float r4[4] = {O.x * inv, O.y * inv, O.z * inv, O.w * inv};
           for (int r = 0; r < world; ++r)
 #pragma unroll
-            for (int e = 0; e < 4; ++e) st_tagged(slots[r] + base + 4 * c + e, r4[e], epoch);
+            for (int e = 0; e < 4; ++e)
+              st_tagged(slots[r] + base + 4 * c + e, r4[e], epoch + 1u);
         }
         if (c0 == 0 && lane < world)
-          st_tagged(slots[lane] + base + D, L > 0.f ? M + __log2f(L) : kNegInf, epoch);
+          st_tagged(slots[lane] + base + D, L > 0.f ? M + __log2f(L) : kNegInf, epoch + 1u);
       }
       __syncthreads();   // s_m / s_l / s_o are rewritten next
     }
@@ -198,6 +203,8 @@ seq_exchange_kernel(const float* __restrict__ o_part, const float* __restrict__ 
 
   // the next kernel in the stream may start launching; it waits for this grid's completion
   pdl_launch_dependents();
+  epoch += 1u;   // this call's epoch
+  const uint64_t* mine = slots[rank] + size_t(epoch & 1u) * set_words;
 
   // ---- phase 2: every rank's state of my items -> the merged fp16 output. Thread d reads
   // every rank's lse word and o word d at once, then polls (time-bounded) only the words that
@@ -241,18 +248,13 @@ seq_exchange_kernel(const float* __restrict__ o_part, const float* __restrict__ 
     }
   }
 
-  // ---- the last CTA to finish publishes this call's epoch
+  // ---- this CTA is done with the call: its next call uses the next epoch (the next kernel
+  // in the stream sees the store once this grid has completed)
   if (my_timeout) timed_out = 1;
   __syncthreads();
   if (tid == 0) {
     if (timed_out) flag_device_error(status, BPT_DEV_WAIT_TIMEOUT);
-    __threadfence();
-    const unsigned done = atomicAdd(&ctl[1], 1u);
-    if (done == gridDim.x - 1) {
-      ctl[1] = 0u;
-      __threadfence();
-      *reinterpret_cast<volatile unsigned*>(ctl) = epoch;
-    }
+    *ctl = epoch;
   }
 }
 
@@ -285,7 +287,7 @@ using namespace bpt;
 extern "C" size_t bpt_seqx_buffer_bytes(int world, int batch, int q_heads, int head_dim) {
   if (world < 1 || batch < 1 || q_heads < 1 || head_dim < 1) return 0;
   const size_t items = size_t(batch) * q_heads;
-  return (2 * size_t(world) * items * slot_words(head_dim) + 32) * 8;
+  return (2 * size_t(world) * items * slot_words(head_dim) + items) * 8;
 }
 
 extern "C" int bpt_seqx_alloc(size_t bytes, void** buf, void* ipc_handle) {
