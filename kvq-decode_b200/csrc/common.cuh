@@ -187,4 +187,27 @@ __host__ __device__ constexpr T cdiv(T a, T b) {
   return (a + b - 1) / b;
 }
 
+// Chunk range [*u0, *u1) of split `split` of S over a sequence of n_units chunks. Unbalanced:
+// the sequence's own chunks are cut into S parts. Balanced: the batch's longest sequence
+// (span_units chunks) is cut into S parts and a shorter sequence keeps the parts that cover
+// it, so every non-empty split of the batch has about span_units / S chunks and a ragged
+// batch launched as one wave has no long-sequence tail (the later splits of short sequences
+// are empty).
+__device__ __forceinline__ void split_range(int split, int S, int n_units, int span_units,
+                                            int* u0, int* u1) {
+  *u0 = min(n_units, int(int64_t(split) * span_units / S));
+  *u1 = min(n_units, int(int64_t(split + 1) * span_units / S));
+}
+
+// Longest sequence of the batch, each length clamped to [0, cap] as the kernels clamp their
+// own. Every warp computes it for itself (no barrier): lane l reads lengths l, l + 32, ...
+__device__ __forceinline__ int batch_max_len(const int32_t* seq_lens, int batch, int64_t cap) {
+  const int lane = threadIdx.x & 31;
+  int m = 0;
+  for (int i = lane; i < batch; i += 32) m = max(m, __ldg(seq_lens + i));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+  return int(min(int64_t(m), cap));
+}
+
 }  // namespace bpt

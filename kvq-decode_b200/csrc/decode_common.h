@@ -25,6 +25,7 @@ struct DecodeParams {
   int batch, q_heads, kv_heads, group, splits, block_size, max_blocks, box_rows;
   int k_c1, v_c1;   // 1: tensor-map dim 1 is the token dim (head-major cache), 0: the head dim
   int final_out;    // 1: a one-split call writes normalised fp16 `out` directly
+  int balance;      // 1: splits sized by the batch's longest sequence (split_range)
   int64_t num_blocks;
   float scale_log2; // softmax scale * log2(e)
 };
@@ -71,6 +72,10 @@ int device_sm_count();
 int plan_splits(int batch, int kv_heads, int block_size, int max_blocks, int sm_count,
                 int resident_per_sm, int chunk_tokens);
 int clamp_splits(int s, int block_size, int max_blocks, int chunk_tokens);
+// Whether a call of batch * kv_heads * splits CTAs, resident_per_sm per SM, uses balanced
+// splits: a batch of several sequences launched as one wave, where the ragged tail of equal
+// per-sequence splits is not hidden by later waves.
+bool balanced_splits(int batch, int kv_heads, int splits, int resident_per_sm);
 
 // cuTensorMapEncodeTiled resolved through the runtime's driver entry-point query (no link
 // dependency on libcuda); null if unavailable.

@@ -31,6 +31,7 @@ namespace bpt {
 namespace {
 
 constexpr int kChunk = 64;          // tokens per pipeline stage
+constexpr int kResidentFp16 = 4;    // tensor-core split CTAs resident per SM (the planner's)
 constexpr int kConsumerWarps = 4;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr float kNegInf = -INFINITY;
@@ -134,8 +135,9 @@ split_kv_fp16_kernel(const __grid_constant__ CUtensorMap tmK,
     n = int(cap);
   }
   const int n_units = cdiv(n, kChunk);
-  const int u0 = int(int64_t(split) * n_units / S);
-  const int u1 = int(int64_t(split + 1) * n_units / S);
+  const int span = p.balance ? cdiv(batch_max_len(p.seq_lens, p.batch, cap), kChunk) : n_units;
+  int u0, u1;
+  split_range(split, S, n_units, span, &u0, &u1);
   const int t_begin = u0 * kChunk;
   const int t_end = min(u1 * kChunk, n);
   const int nchunks = u1 - u0;
@@ -717,6 +719,7 @@ int run_split_fp16(const void* q, int64_t q_sb, int64_t q_sh, const void* k_cach
   p.group = group;
   p.splits = splits;
   p.final_out = final_out;
+  p.balance = balanced_splits(batch, kv_heads, splits, kResidentFp16) ? 1 : 0;
   p.block_size = block_size;
   p.max_blocks = max_blocks;
   p.box_rows = box_rows;

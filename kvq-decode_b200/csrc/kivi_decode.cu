@@ -186,8 +186,9 @@ kivi_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
     n = int(cap);
   }
   const int n_units = cdiv(n, CHUNK);
-  const int u0 = int(int64_t(split) * n_units / S);
-  const int u1 = int(int64_t(split + 1) * n_units / S);
+  const int span = p.balance ? cdiv(batch_max_len(p.seq_lens, p.batch, cap), CHUNK) : n_units;
+  int u0, u1;
+  split_range(split, S, n_units, span, &u0, &u1);
   const int t_begin = u0 * CHUNK;
   const int t_end = min(u1 * CHUNK, n);
   const int nchunks = u1 - u0;
@@ -990,6 +991,11 @@ int run_split_kivi(const bpt_kivi_cache& c, const void* q, int64_t q_sb, int64_t
   p.group = group;
   p.splits = splits;
   p.final_out = final_out;
+  {
+    int kchunk = 0, kresident = 1;
+    kivi_kernel_shape(c.format, group, bs, c.kv_heads, batch, max_blocks, &kchunk, &kresident);
+    p.balance = balanced_splits(batch, c.kv_heads, splits, kresident) ? 1 : 0;
+  }
   p.block_size = bs;
   p.max_blocks = max_blocks;
   p.box_rows = box_rows;

@@ -252,8 +252,9 @@ kivi_tc_decode_kernel(const __grid_constant__ CUtensorMap tmK,
     n = int(cap);
   }
   const int n_units = cdiv(n, CHUNK);
-  const int u0 = int(int64_t(split) * n_units / S);
-  const int u1 = int(int64_t(split + 1) * n_units / S);
+  const int span = p.balance ? cdiv(batch_max_len(p.seq_lens, p.batch, cap), CHUNK) : n_units;
+  int u0, u1;
+  split_range(split, S, n_units, span, &u0, &u1);
   const int t_begin = u0 * CHUNK;
   const int t_end = min(u1 * CHUNK, n);
   const int nchunks = u1 - u0;

@@ -43,10 +43,16 @@ def test_planner_fills_b200():
     from bpt.decode import choose_num_splits, effective_splits
     # B=1, 64k tokens, bs=16: one full wave of 4 CTAs/SM x 148 SMs (8 kv heads x 74 splits)
     assert choose_num_splits(1, 8, 16, 4096, 148) == 74
-    # B=8: still one wave (64 x 9 = 576 <= 592)
+    # B=8: still one wave (64 x 9 = 576 <= 592), splits of at most 8192 tokens
     assert choose_num_splits(8, 8, 16, 1024, 148) == 9
-    # B=64: fewer than 4 splits fit one wave -> ~8 waves of shorter CTAs
-    assert choose_num_splits(64, 8, 16, 4096, 148) == 10
+    # B=64: fewer than 4 splits fit one wave -> just under 7 full waves (8 x 512 = 4096 CTAs)
+    assert choose_num_splits(64, 8, 16, 4096, 148) == 8
+    # B=16 at 64k: 4 splits would fit one wave but be 16k tokens long -> 7 waves (32 splits)
+    assert choose_num_splits(16, 8, 16, 4096, 148) == 32
+    # B=32 at 16k: 7 waves, splits of at least 1024 tokens
+    assert choose_num_splits(32, 8, 16, 1024, 148) == 16
+    # B=1 at 1M tokens: 74 splits would be 14k tokens long -> 7 waves of shorter ones
+    assert choose_num_splits(1, 8, 16, 65536, 148) == 518
     # short context caps the split count (>= 2 chunks of 32 tokens per split)
     assert choose_num_splits(1, 8, 16, 16, 148) == 4
     assert choose_num_splits(1, 8, 16, 2, 148) == 1
@@ -73,10 +79,10 @@ def test_kivi_planner_uses_the_serving_kernels_shape():
     assert f(INT4, 1, 8, 64, 64, 2048, 0, 148) == 74
     # INT4 with batch x kv_heads >= 256 and a block table of >= 32k tokens uses the 3-CTA/SM
     # tcgen05 shape (more splits than INT8); shorter tables and smaller batches keep 2 per SM
-    assert f(INT4, 64, 8, 32, 64, 512, 0, 148) == 7
-    assert f(INT4, 32, 8, 32, 64, 512, 0, 148) == 14
-    assert f(INT4, 32, 8, 32, 64, 128, 0, 148) == 10
-    assert f(INT8, 64, 8, 32, 64, 512, 0, 148) == 5
+    assert f(INT4, 64, 8, 32, 64, 512, 0, 148) == 6
+    assert f(INT4, 32, 8, 32, 64, 512, 0, 148) == 12
+    assert f(INT4, 32, 8, 32, 64, 128, 0, 148) == 8
+    assert f(INT8, 64, 8, 32, 64, 512, 0, 148) == 4
     assert f(INT4, 8, 8, 32, 64, 512, 0, 148) == 4
     # explicit requests are clamped to the 128-token chunk count
     assert f(INT4, 1, 8, 32, 64, 3, 50, 148) == 2

@@ -215,6 +215,27 @@ def test_full_size_batch_against_torch_fp32(B, ctx):
         assert_close(out.float().cpu().numpy(), ref.cpu().numpy(), what=f"B={B} ctx={ctx}")
 
 
+def test_balanced_splits_of_a_very_ragged_batch():
+    """A batch launched as one wave cuts its LONGEST sequence into the splits and gives each
+    shorter sequence only the splits that cover it (empty trailing splits, lse = -inf), so no
+    CTA runs longer than another. Lengths from 0 to 16384 tokens, including one shorter than a
+    chunk, at the planner's count and at explicit counts (all one wave for B=8)."""
+    from bpt import paged_decode_attention
+    from bpt.cache import random_paged_workload
+    from bpt.decode import _sm_count, effective_splits
+    lens = [16384, 1, 0, 16, 9000, 33, 16383, 4096]
+    w = random_paged_workload(lens, 32, 8, 128, 16, "cuda", seed=21, spare_blocks=64)
+    ref = torch_reference(w["q"], w["k_cache"], w["v_cache"], w["block_table"], w["seq_lens"])
+    mb = w["block_table"].shape[1]
+    assert effective_splits(8, 8, 16, mb, None, _sm_count(0)) * 8 * 8 <= 4 * _sm_count(0)
+    for ns in (None, 2, 5, 9):
+        out = paged_decode_attention(w["q"], w["k_cache"], w["v_cache"], w["block_table"],
+                                     w["seq_lens"], num_splits=ns)
+        assert torch.isfinite(out.float()).all()
+        assert_close(out.float().cpu().numpy(), ref.cpu().numpy(), what=f"splits={ns}")
+        assert out[2].abs().max().item() == 0.0   # the empty sequence gives zeros
+
+
 @pytest.mark.parametrize("splits", [1, 4, 9])
 def test_partial_states_and_merges(splits):
     """bpt_decode_fp16_partial + bpt_merge_states give the oracle's per-sequence state

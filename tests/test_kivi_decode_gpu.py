@@ -64,6 +64,7 @@ def test_matches_reference_on_dequantized_cache(name, num_splits):
     (16, 8, 16, [300, 17, 16]),      # group 2, 16-token pages
     (32, 8, 32, [257, 31]),          # 32-token pages
     (32, 8, 128, [700, 129, 128]),   # pages larger than a chunk
+    (32, 8, 64, [4096, 0, 1, 64, 2000, 4095]),   # very ragged: balanced one-wave splits
 ])
 def test_shapes_and_page_sizes(fmt, Hq, Hkv, bs, lens):
     c = kivi.quant_case(7 + bs + Hq, lens, Hq, Hkv, 128, bs, fmt, "spare", 3)
