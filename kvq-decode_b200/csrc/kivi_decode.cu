@@ -34,6 +34,7 @@
 #include "common.cuh"
 #include "decode_common.h"
 #include "mma_decode.cuh"
+#include "split_state.cuh"
 
 namespace bpt {
 namespace kivi {
@@ -67,7 +68,7 @@ struct Cfg {
   static constexpr int NACC = G8 ? 2 : 1;
   static constexpr size_t RING_BYTES = size_t(STAGES) * STAGE_BYTES;
   static constexpr size_t Q_BYTES = 8 * D * 4;             // fp32 q of the group's heads
-  static constexpr size_t MERGE_BYTES = size_t(NCW) * 8 * (D + 2) * 4;
+  static constexpr size_t MERGE_BYTES = size_t(NCW) * 8 * (D + 3) * 4;
   static constexpr size_t BODY_BYTES = RING_BYTES > MERGE_BYTES ? RING_BYTES : MERGE_BYTES;
   static constexpr size_t SMEM_BYTES = 1024 + BODY_BYTES + Q_BYTES + 2 * STAGES * 8 + 64;
 };
@@ -653,30 +654,9 @@ kivi_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
     }
   }
   named_barrier_sync(1, NCW * 32);
-
-  for (int idx = threadIdx.x; idx < p.group * D; idx += NCW * 32) {
-    const int hg = idx / D, d = idx % D;
-    float M = kNegInf;
-#pragma unroll
-    for (int w = 0; w < NCW; ++w) M = fmaxf(M, sM[w * 8 + hg]);
-    float L = 0.f, O = 0.f;
-    if (M != kNegInf) {
-#pragma unroll
-      for (int w = 0; w < NCW; ++w) {
-        const float f = fast_exp2(sM[w * 8 + hg] - M);
-        L = fmaf(sL[w * 8 + hg], f, L);
-        O = fmaf(sAcc[(w * 8 + hg) * D + d], f, O);
-      }
-    }
-    const float o = L > 0.f ? O / L : 0.f;
-    if (S == 1 && p.final_out) {
-      p.out[int64_t(b) * p.o_sb + int64_t(qh0 + hg) * p.o_sh + d] = __float2half_rn(o);
-    } else {
-      const int64_t row = (int64_t(b) * p.q_heads + qh0 + hg) * S + split;
-      p.o_part[row * D + d] = o;
-      if (d == 0) p.lse[row] = L > 0.f ? M + __log2f(L) : kNegInf;
-    }
-  }
+  write_split_state<NCW, D>(sM, sL, sAcc, sAcc + NCW * 8 * D, p, b, qh0, split,
+                            int(threadIdx.x), NCW * 32,
+                            [] { named_barrier_sync(1, NCW * 32); });
 }
 
 #ifndef BPT_KIVI_NCW

@@ -49,7 +49,7 @@ struct ICfg {
   static constexpr int STAGE_FIXED = K_BYTES + V_BYTES + VP_BYTES;
   static constexpr int FQ_ROW = 144;                       // 128 B of limbs + bank padding
   static constexpr int FQ_SLOT = 16 * FQ_ROW;              // 16 limb rows
-  static constexpr size_t MERGE_BYTES = size_t(NW) * 8 * (D + 2) * 4;
+  static constexpr size_t MERGE_BYTES = size_t(NW) * 8 * (D + 3) * 4;
   __host__ __device__ static constexpr int stage_bytes(int nslot) {
     return (STAGE_FIXED + nslot * 512 + 1023) & ~1023;
   }
@@ -635,28 +635,6 @@ kivi_int_decode_kernel(const __grid_constant__ CUtensorMap tmK,
     }
   }
   __syncthreads();
-
-  for (int idx = threadIdx.x; idx < p.group * D; idx += blockDim.x) {
-    const int hg = idx / D, d = idx % D;
-    float M = kNegInf;
-#pragma unroll
-    for (int w = 0; w < NW; ++w) M = fmaxf(M, sM[w * 8 + hg]);
-    float L = 0.f, O = 0.f;
-    if (M != kNegInf) {
-#pragma unroll
-      for (int w = 0; w < NW; ++w) {
-        const float f = fast_exp2(sM[w * 8 + hg] - M);
-        L = fmaf(sL[w * 8 + hg], f, L);
-        O = fmaf(sAcc[(w * 8 + hg) * D + d], f, O);
-      }
-    }
-    const float o = L > 0.f ? O / L : 0.f;
-    if (S == 1 && p.final_out) {
-      p.out[int64_t(b) * p.o_sb + int64_t(qh0 + hg) * p.o_sh + d] = __float2half_rn(o);
-    } else {
-      const int64_t row = (int64_t(b) * p.q_heads + qh0 + hg) * S + split;
-      p.o_part[row * D + d] = o;
-      if (d == 0) p.lse[row] = L > 0.f ? M + __log2f(L) : kNegInf;
-    }
-  }
+  write_split_state<NW, D>(sM, sL, sAcc, sAcc + NW * 8 * D, p, b, qh0, split, int(threadIdx.x),
+                           int(blockDim.x), [] { __syncthreads(); });
 }

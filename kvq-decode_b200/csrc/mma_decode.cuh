@@ -26,6 +26,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "split_state.cuh"
 #include "decode_common.h"
 
 namespace bpt {
@@ -402,74 +403,9 @@ split_kv_fp16_mma_kernel(const __grid_constant__ CUtensorMap tmK,
     }
   }
   named_barrier_sync(1, NCW * 32);
-  // Per q head, once (consumer thread hg): each warp's weight 2^(m_w - M) / L and the split's
-  // lse. The epilogue of the split that ends last is on the call's critical path, and the
-  // per-element form (max, exp2 and a division for every element) took ~1.7 us there, with
-  // the other CTAs of the SM still streaming.
-  float* sF = sAcc + NCW * 8 * D;   // [8 q heads][NCW]
-  if (threadIdx.x < p.group) {
-    const int hg = threadIdx.x;
-    float M = kNegInf;
-#pragma unroll
-    for (int w = 0; w < NCW; ++w) M = fmaxf(M, sM[w * 8 + hg]);
-    float f[NCW], L = 0.f;
-#pragma unroll
-    for (int w = 0; w < NCW; ++w) {
-      f[w] = M != kNegInf ? fast_exp2(sM[w * 8 + hg] - M) : 0.f;
-      L = fmaf(sL[w * 8 + hg], f[w], L);
-    }
-    const float inv = L > 0.f ? 1.f / L : 0.f;
-#pragma unroll
-    for (int w = 0; w < NCW; ++w) sF[hg * NCW + w] = f[w] * inv;
-    if (!(S == 1 && p.final_out))
-      p.lse[(int64_t(b) * p.q_heads + qh0 + hg) * S + split] =
-          L > 0.f ? M + __log2f(L) : kNegInf;
-  }
-  named_barrier_sync(1, NCW * 32);
-  // every element: the weighted sum of the warps' accumulators, 4 channels per thread, stored
-  // as one vector where the destination's alignment allows it (caller partial buffers may be
-  // offset views)
-  const bool out_vec = (reinterpret_cast<uintptr_t>(p.out) & 7) == 0 && p.o_sb % 4 == 0 &&
-                       p.o_sh % 4 == 0;
-  const bool part_vec = (reinterpret_cast<uintptr_t>(p.o_part) & 15) == 0;
-  for (int idx = 4 * int(threadIdx.x); idx < p.group * D; idx += 4 * NCW * 32) {
-    const int hg = idx / D, d = idx % D;
-    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int w = 0; w < NCW; ++w) {
-      const float fw = sF[hg * NCW + w];
-      const float4 a = *reinterpret_cast<const float4*>(sAcc + (w * 8 + hg) * D + d);
-      o.x = fmaf(a.x, fw, o.x);
-      o.y = fmaf(a.y, fw, o.y);
-      o.z = fmaf(a.z, fw, o.z);
-      o.w = fmaf(a.w, fw, o.w);
-    }
-    if (S == 1 && p.final_out) {
-      __half* dst = p.out + int64_t(b) * p.o_sb + int64_t(qh0 + hg) * p.o_sh + d;
-      const __half2 h01 = __floats2half2_rn(o.x, o.y), h23 = __floats2half2_rn(o.z, o.w);
-      if (out_vec) {
-        uint2 pk;
-        pk.x = *reinterpret_cast<const uint32_t*>(&h01);
-        pk.y = *reinterpret_cast<const uint32_t*>(&h23);
-        *reinterpret_cast<uint2*>(dst) = pk;
-      } else {
-        dst[0] = __low2half(h01);
-        dst[1] = __high2half(h01);
-        dst[2] = __low2half(h23);
-        dst[3] = __high2half(h23);
-      }
-    } else {
-      float* dst = p.o_part + ((int64_t(b) * p.q_heads + qh0 + hg) * S + split) * D + d;
-      if (part_vec) {
-        *reinterpret_cast<float4*>(dst) = o;
-      } else {
-        dst[0] = o.x;
-        dst[1] = o.y;
-        dst[2] = o.z;
-        dst[3] = o.w;
-      }
-    }
-  }
+  write_split_state<NCW, D>(sM, sL, sAcc, sAcc + NCW * 8 * D, p, b, qh0, split,
+                            int(threadIdx.x), NCW * 32,
+                            [] { named_barrier_sync(1, NCW * 32); });
 }
 
 template <int D, int NCW, int STAGES, int MINB, bool G8>
