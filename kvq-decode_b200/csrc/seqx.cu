@@ -51,9 +51,11 @@ namespace bpt {
 namespace {
 
 constexpr int kMaxRanks = 8;
-constexpr int kWarps = 8;
+// few rows per warp: each warp's online merge is a serial chain per row (as in the split
+// merge of decode_fp16.cu)
+constexpr int kWarps = 16;   // 512 threads: the second phase keeps its words in registers
 constexpr int kThreads = 32 * kWarps;
-constexpr int kRows = 16;   // split rows a warp loads before using any
+constexpr int kRows = 8;    // split rows a warp loads before using any
 constexpr float kNegInf = -INFINITY;
 
 struct RankBufs {
@@ -100,7 +102,7 @@ seq_exchange_kernel(const float* __restrict__ o_part, const float* __restrict__ 
                     int q_heads, int splits, int D, RankBufs bufs, int world, int rank,
                     __half* __restrict__ out, int64_t o_sb, int64_t o_sh, unsigned* status,
                     uint64_t budget_ns) {
-  __shared__ float s_m[kWarps], s_l[kWarps];
+  __shared__ float s_m[kWarps], s_l[kWarps], s_f[kWarps];
   __shared__ float4 s_o[kWarps][32];
   __shared__ int timed_out;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -117,9 +119,10 @@ seq_exchange_kernel(const float* __restrict__ o_part, const float* __restrict__ 
   if (tid == 0) timed_out = 0;
 
   // ---- phase 1: local split merge, epoch-tagged stores into every rank's slot (rank, item).
-  // Warp w owns splits w, w + 8, ... and merges them online in batches of kRows rows, every
+  // Warp w owns splits w, w + 16, ... and merges them online in batches of kRows rows, every
   // load of a batch (the rows' lse and this lane's 4 channels of their o) issued before any is
-  // used; the 8 warp states are combined in warp order through shared memory.
+  // used; the 16 warp states are combined in warp order through shared memory, lane w of
+  // warp 0 turning state w into its weight 2^(m_w - M) / L once.
   for (int it = blockIdx.x; it < items; it += gridDim.x) {
     const float* l = lse + int64_t(it) * splits;
     const float* o = o_part + int64_t(it) * splits * D;
@@ -167,28 +170,31 @@ seq_exchange_kernel(const float* __restrict__ o_part, const float* __restrict__ 
       s_o[warp][lane] = acc;
       __syncthreads();
       if (warp == 0) {
-        float M = kNegInf;
+        const float mw = lane < kWarps ? s_m[lane] : kNegInf;   // lane w: state w
+        float M = mw;
 #pragma unroll
-        for (int w = 0; w < kWarps; ++w) M = fmaxf(M, s_m[w]);
-        float L = 0.f;
+        for (int off = 16; off > 0; off >>= 1)
+          M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+        const float fw = (lane < kWarps && M != kNegInf) ? fast_exp2(mw - M) : 0.f;
+        float L = lane < kWarps ? s_l[lane] * fw : 0.f;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+        if (lane < kWarps) s_f[lane] = L > 0.f ? fw / L : 0.f;
+        __syncwarp();
         float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (M != kNegInf) {
-#pragma unroll
-          for (int w = 0; w < kWarps; ++w) {
-            const float f = fast_exp2(s_m[w] - M);
-            const float4 a4 = s_o[w][lane];
-            L = fmaf(s_l[w], f, L);
-            O.x = fmaf(a4.x, f, O.x);
-            O.y = fmaf(a4.y, f, O.y);
-            O.z = fmaf(a4.z, f, O.z);
-            O.w = fmaf(a4.w, f, O.w);
-          }
+#pragma unroll 8
+        for (int w = 0; w < kWarps; ++w) {
+          const float f = s_f[w];
+          const float4 a4 = s_o[w][lane];
+          O.x = fmaf(a4.x, f, O.x);
+          O.y = fmaf(a4.y, f, O.y);
+          O.z = fmaf(a4.z, f, O.z);
+          O.w = fmaf(a4.w, f, O.w);
         }
-        const float inv = L > 0.f ? 1.f / L : 0.f;
         const size_t base =
             size_t((epoch + 1u) & 1u) * set_words + (size_t(rank) * items + it) * slot_words(D);
         if (c_in) {
-          const float r4[4] = {O.x * inv, O.y * inv, O.z * inv, O.w * inv};
+          const float r4[4] = {O.x, O.y, O.z, O.w};
           for (int r = 0; r < world; ++r)
 #pragma unroll
             for (int e = 0; e < 4; ++e)
