@@ -172,6 +172,14 @@ kivi_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = p.splits;
 
+  // the tensor maps are kernel parameters, not written by the previous kernel: their fetch
+  // overlaps the wait
+  if (threadIdx.x == 0) {
+    prefetch_tensormap(&tmK);
+    prefetch_tensormap(&tmV);
+    prefetch_tensormap(&tmKS);
+    if (!FP8) prefetch_tensormap(&tmKZ);
+  }
   // launched as a programmatic dependent of the previous kernel in the stream: nothing that
   // kernel may write (q, the cache, the table, the lengths, the workspace) is read before
   // it completed
@@ -228,12 +236,6 @@ kivi_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
 
   if (warp == NCW) {
     // ------------------------------------------------------------------ producer warp
-    if (lane == 0) {
-      prefetch_tensormap(&tmK);
-      prefetch_tensormap(&tmV);
-      prefetch_tensormap(&tmKS);
-      if (!FP8) prefetch_tensormap(&tmKZ);
-    }
     const uint64_t pol = l2_evict_first_policy();
     const int32_t* bt = p.block_table + int64_t(b) * p.bt_sb;
     const int R = p.box_rows;                 // min(block_size, CHUNK)

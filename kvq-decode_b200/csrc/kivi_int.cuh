@@ -137,6 +137,14 @@ kivi_int_decode_kernel(const __grid_constant__ CUtensorMap tmK,
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = p.splits;
 
+  // the tensor maps are kernel parameters, not written by the previous kernel: their fetch
+  // overlaps the wait
+  if (threadIdx.x == 0) {
+    prefetch_tensormap(&tmK);
+    prefetch_tensormap(&tmV);
+    prefetch_tensormap(&tmKS);
+    prefetch_tensormap(&tmKZ);
+  }
   // launched as a programmatic dependent of the previous kernel in the stream: nothing that
   // kernel may write (q, the cache, the table, the lengths, the workspace) is read before
   // it completed
@@ -215,12 +223,6 @@ kivi_int_decode_kernel(const __grid_constant__ CUtensorMap tmK,
   int win = (win_base + lane <= last_page) ? __ldg(bt + win_base + lane) : 0;
   const uint64_t pol = l2_evict_first_policy();
   const uint32_t box_bytes = uint32_t(R) * C::K_ROW + uint32_t(INT4 ? R / 2 : R) * 128u + 512u;
-  if (threadIdx.x == 0) {
-    prefetch_tensormap(&tmK);
-    prefetch_tensormap(&tmV);
-    prefetch_tensormap(&tmKS);
-    prefetch_tensormap(&tmKZ);
-  }
 
   // every thread calls issue() for the same chunks in the same order (identical windows)
   auto issue = [&](int cc) {

@@ -136,6 +136,12 @@ split_kv_fp16_mma_kernel(const __grid_constant__ CUtensorMap tmK,
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = p.splits;
 
+  // the tensor maps are kernel parameters, not written by the previous kernel: their fetch
+  // overlaps the wait
+  if (warp == NCW && lane == 0) {
+    prefetch_tensormap(&tmK);
+    prefetch_tensormap(&tmV);
+  }
   // launched as a programmatic dependent of the previous kernel in the stream: nothing that
   // kernel may write (q, the cache, the table, the lengths, the workspace) is read before
   // it completed
@@ -187,10 +193,6 @@ split_kv_fp16_mma_kernel(const __grid_constant__ CUtensorMap tmK,
 
   if (warp == NCW) {
     // ------------------------------------------------------------------ producer warp
-    if (lane == 0) {
-      prefetch_tensormap(&tmK);
-      prefetch_tensormap(&tmV);
-    }
     const uint64_t pol = l2_evict_first_policy();
     const int32_t* bt = p.block_table + int64_t(b) * p.bt_sb;
     const int R = p.box_rows;                     // min(block_size, CHUNK)
