@@ -51,7 +51,11 @@ const char* bpt_status_string(int status);
 int bpt_version(void);
 
 /* Number of KV splits the heuristic picks. Replaces choose_num_splits
- * (src/bpt/triton_fp16.py:175-180); B200 tuning (148 SMs, 64-token chunks). */
+ * (src/bpt/triton_fp16.py:175-180); B200 tuning: one wave of CTAs when at least 4 splits fit
+ * in it and they stay at most 8192 tokens of the table long, otherwise just under 7 full
+ * waves of splits of at least 1024 tokens. A multi-sequence batch launched as one wave cuts
+ * its longest sequence into the splits and every other sequence keeps the splits that cover
+ * it (its later splits are empty); otherwise each sequence's own tokens are cut evenly. */
 int bpt_plan_splits(int batch, int kv_heads, int block_size, int max_blocks, int sm_count);
 
 /* Split count a decode call actually uses for a requested num_splits (<= 0 = heuristic),
