@@ -14,16 +14,9 @@ constexpr int kChunkTokens = 32;    // tokens per pipeline stage of the decode k
 constexpr int kResidentCtas = 4;    // decode CTAs resident per SM
 constexpr int kMinChunksPerSplit = 2;
 constexpr int kMinSingleWaveSplits = 4;
-#ifndef BPT_PLANNER
-#define BPT_PLANNER 1
-#endif
-#if BPT_PLANNER
 constexpr int kWaves = 7;                      // several-wave plans: just under 7 full waves
 constexpr int64_t kMaxSingleWaveTokens = 8192; // longest split of a one-wave plan
 constexpr int64_t kMinMultiWaveTokens = 1024;  // shortest split of a several-wave plan
-#else
-constexpr int kWaves = 8;
-#endif
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
@@ -125,15 +118,14 @@ int plan_splits(int batch, int kv_heads, int block_size, int max_blocks, int sm_
   const int64_t work = int64_t(batch > 0 ? batch : 1) * (kv_heads > 0 ? kv_heads : 1);
   const int64_t resident = int64_t(sm_count) * resident_per_sm;
   int64_t want = resident / work;
-#if BPT_PLANNER
   // ONE wave when at least 4 splits fit in it and its splits stay at most 8192 tokens of the
   // table: every CTA starts together, and a ragged batch is balanced by cutting the longest
   // sequence (split_range), so no CTA runs much longer than the others. Otherwise just under
   // 7 full waves of shorter CTAs (floor, so the last wave is nearly full: a last wave of a
   // few CTAs cannot keep HBM busy), with splits of at least 1024 tokens. Measured on B200
   // (ragged FP16 batches, lengths U[0.75, 1] ctx): B=16/64k 4 splits 604 us vs 32 splits
-  // 557 us; B=32/64k 19 splits 1180 us vs 16 splits 1123 us; B=64/64k 10 vs 8 splits
-  // 2306 vs 2246 us (one box).
+  // 556 us; B=32/64k 19 splits 1135 us vs 16 splits 1102 us; B=64/64k 10 vs 8 splits
+  // 2190 vs 2169 us (one box, the two planners alternated).
   const int64_t span_tokens = units * chunk_tokens;
   if (want < kMinSingleWaveSplits || span_tokens > kMaxSingleWaveTokens * want) {
     const int64_t one_wave = want;
@@ -143,12 +135,6 @@ int plan_splits(int batch, int kv_heads, int block_size, int max_blocks, int sm_
     const int64_t most = span_tokens / kMinMultiWaveTokens;
     if (want > most) want = most > one_wave ? most : one_wave;
   }
-#else
-  // If at least 4 splits still fit in ONE wave, use exactly that many (every CTA starts
-  // together, no tail); otherwise aim for ~8 waves of shorter CTAs so the ragged tail is
-  // small. Never split below 2 chunks per split.
-  if (want < kMinSingleWaveSplits) want = (kWaves * resident + work - 1) / work;
-#endif
   int64_t cap = units / kMinChunksPerSplit;
   if (cap < 1) cap = 1;
   if (want > cap) want = cap;
@@ -156,14 +142,11 @@ int plan_splits(int batch, int kv_heads, int block_size, int max_blocks, int sm_
   return int(want);
 }
 
-// 0: never balance, 1: balance a multi-sequence batch launched as one wave, 2: always
-#ifndef BPT_BALANCE_MODE
-#define BPT_BALANCE_MODE 1
-#endif
-
+// Balanced splits for a multi-sequence batch launched as one wave. Several-wave launches keep
+// equal per-sequence splits (the block scheduler fills their tail; balancing them measured
+// slower on B200: B=64/64k 2211 -> 2316 us).
 bool balanced_splits(int batch, int kv_heads, int splits, int resident_per_sm) {
-  if (BPT_BALANCE_MODE == 0 || batch < 2) return false;
-  if (BPT_BALANCE_MODE == 2) return true;
+  if (batch < 2) return false;
   return int64_t(batch) * kv_heads * splits <= int64_t(device_sm_count()) * resident_per_sm;
 }
 
