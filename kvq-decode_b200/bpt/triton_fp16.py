@@ -11,7 +11,8 @@ planner (CTAs resident per SM, minimum tokens per split).
 from .decode import _sm_count, choose_num_splits, paged_decode_attention
 
 # reference: src/bpt/triton_fp16.py:166-167 (values are the B200 planner's: one wave of
-# 4 resident CTAs per SM when >= 4 splits fit, else ~8 waves; >= 2 chunks of 32 tokens)
+# 4 resident CTAs per SM when >= 4 splits of at most 8192 tokens fit, else just under 7
+# waves; >= 2 chunks of 32 tokens)
 TARGET_PROGRAMS_PER_SM = 4
 MIN_TOKENS_PER_SPLIT = 64
 
